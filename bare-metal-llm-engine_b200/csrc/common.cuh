@@ -1,0 +1,294 @@
+// common.cuh -- shared host and device machinery for the B200 hot-path library.
+//
+// Host side: the C-ABI error convention (status codes plus a thread-local
+// message, mirroring the reference's ENGINE_CHECK / CUDA_CHECK /
+// CUDA_CHECK_KERNEL in include/engine/check.hpp:36-107), device property
+// caches, and the driver entry point for TMA tensor-map encoding.
+//
+// Device side: thin inline-PTX wrappers for the sm_100a features the kernels
+// use -- mbarriers with BOUNDED waits, TMA tiled loads, tcgen05 (TMEM
+// allocation, UMMA issue, commit, TMEM loads) -- and the device error word that
+// a kernel sets instead of hanging when a wait runs out.
+#pragma once
+
+#include <cuda.h>  // CUtensorMap and enums only; libcuda is reached via cudaGetDriverEntryPoint
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/engine_b200.h"
+
+namespace b200 {
+
+// ------------------------------------------------------------------ host side
+
+/// Records `msg` as this thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+/// Records a CUDA runtime error with its name and string, returns ENGINE_ERR_CUDA.
+int set_cuda_error(cudaError_t err, const char* what);
+
+/// Post-launch check: launch errors always; with ENGINE_ALWAYS_SYNC_CHECK=1 in the
+/// environment it also synchronises the device and surfaces execution faults and
+/// device-side wait timeouts (the reference's debug-build CUDA_CHECK_KERNEL).
+int check_launch(const char* what);
+
+bool always_sync_check();
+int sm_count();            // current device
+int max_smem_optin();      // current device, bytes
+/// Device error word of the current device (timeouts set bits here).
+unsigned int* device_error_word();
+/// Wait limit for every bounded device-side spin, in nanoseconds.
+unsigned long long wait_limit_ns();
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+/// 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes`, row pitch
+/// `ld` elements, box `box_rows` x `box_cols`, 128-byte swizzle.  Cached per
+/// (pointer, shape, box); returns false (with the error recorded) on failure.
+bool make_tmap_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+                  uint32_t box_cols);
+
+}  // namespace b200
+
+#define B200_REQUIRE(cond, msg)                                      \
+  do {                                                               \
+    if (!(cond)) return ::b200::set_error(ENGINE_ERR_INVALID, (msg)); \
+  } while (0)
+
+#define B200_CUDA(call)                                           \
+  do {                                                            \
+    cudaError_t b200_e_ = (call);                                 \
+    if (b200_e_ != cudaSuccess) return ::b200::set_cuda_error(b200_e_, #call); \
+  } while (0)
+
+#define B200_ENTRY_BEGIN try {
+#define B200_ENTRY_END                                                     \
+  }                                                                        \
+  catch (const std::exception& e) {                                        \
+    return ::b200::set_error(ENGINE_ERR_INTERNAL, e.what());              \
+  }                                                                        \
+  catch (...) {                                                            \
+    return ::b200::set_error(ENGINE_ERR_INTERNAL, "unknown C++ exception"); \
+  }
+
+// ---------------------------------------------------------------- device side
+
+namespace b200 {
+
+// Bits of the device error word.
+constexpr unsigned int kErrWaitTimeout = 1u;   // an mbarrier / cluster wait ran out
+constexpr unsigned int kErrBadArgument = 2u;   // a kernel's own bounds check fired
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// ---- mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+/// Waits for the phase of parity `parity` of `bar` to complete.  Returns false
+/// (after setting kErrWaitTimeout in `err`) if it has not completed within
+/// `limit_ns` nanoseconds of the first failed poll.  Never spins without limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns, unsigned int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long deadline = globaltimer() + limit_ns;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 63u && globaltimer() > deadline) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ---- TMA (no multicast anywhere in this library)
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
+                                            uint64_t* bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map,
+                                                 uint64_t* bar, int32_t x, int32_t y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- tcgen05 / TMEM
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+/// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (FP16 or BF16 in, FP32 acc).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+/// Arrives once on `bar` when all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+/// 32 lanes x 32 columns of 32-bit from TMEM: thread i of the warp receives
+/// lane (base_lane + i), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// ---- UMMA descriptors (tcgen05 shared-memory matrix descriptor, sm_100 format)
+//
+// bits [0,14)  start address >> 4        bits [16,30) leading byte offset >> 4
+// bits [32,46) stride byte offset >> 4   bits [46,48) version = 1
+// bits [49,52) base offset (0)           bit  52      LBO mode (0)
+// bits [61,64) layout: 0 none, 2 = 128B swizzle, 4 = 64B, 6 = 32B
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+/// Instruction descriptor for kind::f16: FP32 accumulate, A/B FP16 (bf16=false)
+/// or BF16 (bf16=true), dense, no negation; a_mn / b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool bf16, bool a_mn,
+                                                      bool b_mn) {
+  return (1u << 4)                                   // D format F32
+         | ((bf16 ? 1u : 0u) << 7)                   // A format
+         | ((bf16 ? 1u : 0u) << 10)                  // B format
+         | ((a_mn ? 1u : 0u) << 15)                  // A major
+         | ((b_mn ? 1u : 0u) << 16)                  // B major
+         | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+}  // namespace b200

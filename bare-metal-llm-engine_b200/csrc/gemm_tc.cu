@@ -1,0 +1,640 @@
+// gemm_tc.cu -- FP16 / BF16 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+//   C[M,N] = A[M,K] * op(B) (+ residual),   FP32 accumulation in TMEM,
+//   op(B) = B[K,N] (row-major, "MN-major" UMMA operand; the legacy matmul layout)
+//        or W[N,K]^T (K-major operand; the activation x weight projection layout).
+//
+// One CTA per SM (persistent over output tiles), 192 threads in three roles:
+//   warp 0      one elected thread issues TMA tiled loads (128-byte swizzle, no
+//               multicast) of a 128x64 A tile and a BNx64 B tile per stage into a
+//               multi-stage shared-memory ring guarded by full/empty mbarriers;
+//   warp 1      allocates TMEM (2 accumulators x BN fp32 columns) and one thread
+//               issues tcgen05.mma (M=128, N=BN, K=16, four per 64-wide k-block),
+//               committing each stage back to the producer and each finished
+//               accumulator to the epilogue;
+//   warps 2..5  read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+//               32*(w%4)..+31, i.e. tile rows), add the residual in FP32, round
+//               once to the 16-bit type and store -- while the MMA warp already
+//               accumulates the next tile into the other TMEM buffer.
+//
+// Two further modes serve the small-batch projections (the HBM-bound decode
+// configurations) without a second kernel:
+//   SWAP  the weight W[N,K] is the UMMA "A" operand (128 weight rows per tile)
+//         and the few activation rows are the "B" operand (N = 16..64), so a
+//         batch of 16 still uses a full-height MMA; the epilogue writes the
+//         transposed tile back into Y[M,N] (lanes = consecutive n: coalesced);
+//   SPLIT the K range of each tile is divided over S CTAs of one thread-block
+//         cluster (S <= 8) so that 48 weight tiles still cover all SMs; each CTA
+//         parks its FP32 partial in shared memory and the partials are summed
+//         in fixed rank order through distributed shared memory.
+//   HILO  (with SWAP) the activation operand holds each row twice -- its FP16
+//         rounding and the FP16 rounding of the remainder -- and the epilogue
+//         adds the two accumulator columns, so an FP32 activation (the fused
+//         RMSNorm output) is multiplied at ~FP32 accuracy.
+//
+// Every mbarrier wait is bounded (ENGINE_WAIT_TIMEOUT_MS, default 2 s): on expiry
+// the thread sets the device error word, abandons its loop and proceeds to the
+// common teardown, where TMEM is released.
+#include <cooperative_groups.h>
+
+#include <atomic>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace b200 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 x 16-bit = 128 bytes: one 128B-swizzle row
+constexpr int kThreads = 192;
+
+struct TcParams {
+  int64_t K;
+  int64_t num_kb;        // ceil(K / 64)
+  int64_t kb_per_split;  // k-blocks per cluster rank
+  int tiles_m, tiles_n;  // tile grid over (A rows, B rows)
+  int split;             // S: CTAs per cluster along K (1 = no split)
+  void* out;
+  const void* resid;
+  int64_t ldo;           // row pitch (elements) of out and resid
+  int64_t out_rows;      // M of Y / C
+  int64_t out_cols;      // N of Y / C
+  int half_b;            // HILO: columns [half_b, 2*half_b) hold the remainders
+  int vec_out;           // 16-byte output stores allowed
+  unsigned int* err;
+  unsigned long long limit_ns;
+};
+
+constexpr int pow2_at_least(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int BN>
+struct TcCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 10));
+  static constexpr int kTmemCols = pow2_at_least(2 * BN);
+  static constexpr int kPartialPitch = BN + 4;  // floats per row of the split-K partial
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static_assert(kStages * kStageBytes >= kBM * kPartialPitch * 4, "partial must fit");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float load16(const void* p, int64_t i) {
+  if constexpr (BF16) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  } else {
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ void store16(void* p, int64_t i, float v) {
+  if constexpr (BF16) {
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  }
+}
+
+__device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm,
+                                            int& tn) {
+  constexpr int G = 8;  // walk G row-tiles at a time so B tiles are reused from L2
+  const int64_t per_group = static_cast<int64_t>(G) * tiles_n;
+  const int64_t group = t / per_group;
+  const int first_m = static_cast<int>(group * G);
+  const int gsize = (tiles_m - first_m < G) ? tiles_m - first_m : G;
+  const int64_t r = t % per_group;
+  tm = first_m + static_cast<int>(r % gsize);
+  tn = static_cast<int>(r / gsize);
+}
+
+/// Writes one output element of the tile: (rl, j) = (tile row, tile column).
+template <bool SWAP, bool RESID, bool BF16>
+__device__ __forceinline__ void emit(const TcParams& p, int tm, int tn, int rl, int j, int bn,
+                                     float v) {
+  int64_t r, c;
+  if constexpr (SWAP) {
+    c = static_cast<int64_t>(tm) * kBM + rl;  // weight row -> output column
+    r = static_cast<int64_t>(tn) * bn + j;    // activation row -> output row
+  } else {
+    r = static_cast<int64_t>(tm) * kBM + rl;
+    c = static_cast<int64_t>(tn) * bn + j;
+  }
+  if (r >= p.out_rows || c >= p.out_cols) return;
+  const int64_t idx = r * p.ldo + c;
+  if constexpr (RESID) v = v + load16<BF16>(p.resid, idx);
+  store16<BF16>(p.out, idx, v);
+}
+
+template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                   const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+  using Cfg = TcCfg<BN>;
+  constexpr int ST = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t num_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  const int z = static_cast<int>(blockIdx.z);
+  const int64_t kb0 = static_cast<int64_t>(z) * p.kb_per_split;
+  const int64_t kb1 = (kb0 + p.kb_per_split < p.num_kb) ? kb0 + p.kb_per_split : p.num_kb;
+  const bool have_k = kb1 > kb0;
+  const int64_t t_begin = blockIdx.x;
+  const int64_t t_step = (p.split > 1) ? num_tiles : gridDim.x;  // split: one tile per CTA
+
+  constexpr uint32_t kIdesc = umma_idesc_f16(kBM, BN, BF16, false, B_MN);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && have_k) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = t_begin; ok && t < num_tiles; t += t_step) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t s = it % ST;
+          const uint32_t ph = (it / ST) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.limit_ns, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          tma_load_2d(sa, &tmA, &full[s], static_cast<int32_t>(kb * kBK), tm * kBM);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_2d(sb + j * 8192, &tmB, &full[s], tn * BN + j * 64,
+                          static_cast<int32_t>(kb * kBK));
+            }
+          } else {
+            tma_load_2d(sb, &tmB, &full[s], static_cast<int32_t>(kb * kBK), tn * BN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      for (int64_t t = t_begin; ok && t < num_tiles; t += t_step, ++tl) {
+        const uint32_t a = tl & 1u;
+        const uint32_t aph = (tl >> 1) & 1u;
+        if (!mbar_wait(&tempty[a], aph ^ 1u, p.limit_ns, p.err)) break;
+        tc_fence_after();
+        if (!have_k) {  // empty K range of this cluster rank: the partial is zero
+          mbar_arrive(&tfull[a]);
+          continue;
+        }
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t s = it % ST;
+          const uint32_t ph = (it / ST) & 1u;
+          if (!mbar_wait(&full[s], ph, p.limit_ns, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = umma_desc_sw128(sa + kk * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_MN) {
+              bdesc = umma_desc_sw128(sb + kk * 2048, 8192, 1024);
+            } else {
+              bdesc = umma_desc_sw128(sb + kk * 32, 16, 1024);
+            }
+            umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[a]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int rl = q * 32 + lane;
+    uint32_t tl = 0;
+    for (int64_t t = t_begin; t < num_tiles; t += t_step, ++tl) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const uint32_t a = tl & 1u;
+      const uint32_t aph = (tl >> 1) & 1u;
+      if (!mbar_wait(&tfull[a], aph, p.limit_ns, p.err)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
+
+      if (p.split > 1) {
+        // Park the FP32 partial in shared memory (the pipeline ring is idle now).
+        float* P = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(taddr + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            P[rl * Cfg::kPartialPitch + c + i] = have_k ? __uint_as_float(v[i]) : 0.0f;
+        }
+      } else if constexpr (SWAP) {
+        if constexpr (HILO) {
+          // Columns j and j + half_b hold the two parts of activation row j.
+          const int hb = p.half_b;
+          float f[BN];
+#pragma unroll
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(taddr + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) f[c + i] = __uint_as_float(v[i]);
+          }
+#pragma unroll
+          for (int j = 0; j < BN / 2; ++j) {
+            if (j < hb) emit<true, RESID, BF16>(p, tm, tn, rl, j, BN, f[j] + f[j + hb]);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(taddr + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              emit<true, RESID, BF16>(p, tm, tn, rl, c + i, BN, __uint_as_float(v[i]));
+          }
+        }
+      } else {
+        const int64_t row = static_cast<int64_t>(tm) * kBM + rl;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_wait_ld();
+          const int64_t col0 = static_cast<int64_t>(tn) * BN + c;
+          if (row < p.out_rows) {
+            float f[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+            if (p.vec_out && col0 + 32 <= p.out_cols) {
+              const int64_t base = row * p.ldo + col0;
+              if constexpr (RESID) {
+                const uint4* rp = reinterpret_cast<const uint4*>(
+                    reinterpret_cast<const uint16_t*>(p.resid) + base);
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                  const uint4 rv = rp[g];
+                  const uint16_t* rh = reinterpret_cast<const uint16_t*>(&rv);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) {
+                    float r;
+                    if constexpr (BF16) {
+                      r = __uint_as_float(static_cast<uint32_t>(rh[i]) << 16);
+                    } else {
+                      r = __half2float(__ushort_as_half(rh[i]));
+                    }
+                    f[g * 8 + i] += r;
+                  }
+                }
+              }
+              uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + base);
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                uint4 o;
+                o.x = pack2<BF16>(f[g * 8 + 0], f[g * 8 + 1]);
+                o.y = pack2<BF16>(f[g * 8 + 2], f[g * 8 + 3]);
+                o.z = pack2<BF16>(f[g * 8 + 4], f[g * 8 + 5]);
+                o.w = pack2<BF16>(f[g * 8 + 6], f[g * 8 + 7]);
+                op[g] = o;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) emit<false, RESID, BF16>(p, tm, tn, rl, c + i, BN, f[i]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[a]);
+    }
+  }
+
+  __syncthreads();
+
+  if (p.split > 1) {
+    // Sum the S partials of this tile in rank order; CTA z finishes rows z, z+S, ...
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    int tm, tn;
+    tile_coords(t_begin, p.tiles_m, p.tiles_n, tm, tn);
+    const float* P = reinterpret_cast<const float*>(smem);
+    const int S = p.split;
+    const int my_rows = (kBM - z + S - 1) / S;
+    const int cols = HILO ? p.half_b : BN;
+    for (int e = threadIdx.x; e < my_rows * cols; e += kThreads) {
+      const int r = z + S * (e / cols);
+      const int j = e % cols;
+      float v = 0.0f;
+      for (int qr = 0; qr < S; ++qr) {
+        const float* peer = cluster.map_shared_rank(P, qr);
+        v += peer[r * Cfg::kPartialPitch + j];
+        if constexpr (HILO) v += peer[r * Cfg::kPartialPitch + j + p.half_b];
+      }
+      emit<SWAP, RESID, BF16>(p, tm, tn, r, j, BN, v);
+    }
+    cluster.sync();
+  }
+
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int grid_x,
+              cudaStream_t stream) {
+  using Cfg = TcCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, B_MN, SWAP, HILO, RESID, BF16>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((configured.load() & bit) == 0) {
+    B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg::kSmemBytes));
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(p.split));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = static_cast<unsigned>(p.split);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  return ENGINE_OK;
+}
+
+template <int BN, bool B_MN, bool SWAP, bool HILO, bool BF16>
+int launch_tc_r(bool resid, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
+                int grid_x, cudaStream_t stream) {
+  return resid ? launch_tc<BN, B_MN, SWAP, HILO, true, BF16>(ta, tb, p, grid_x, stream)
+               : launch_tc<BN, B_MN, SWAP, HILO, false, BF16>(ta, tb, p, grid_x, stream);
+}
+
+int env_int(const char* name, int dflt) {
+  const char* e = std::getenv(name);
+  if (e == nullptr || e[0] == '\0') return dflt;
+  return static_cast<int>(std::strtol(e, nullptr, 10));
+}
+
+// 16-bit GEMM on CUDA cores for shapes TMA cannot describe (row pitch not a
+// multiple of 16 bytes, misaligned base).  FP32 accumulate; same epilogue rules.
+template <bool BF16>
+__global__ void __launch_bounds__(256) gemm16_simt_kernel(const void* __restrict__ A,
+                                                          const void* __restrict__ B,
+                                                          const void* __restrict__ R,
+                                                          void* __restrict__ C, int64_t M,
+                                                          int64_t N, int64_t K, int b_kmajor) {
+  __shared__ float As[16][17];
+  __shared__ float Bs[16][17];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t row = static_cast<int64_t>(blockIdx.y) * 16 + ty;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * 16 + tx;
+  float acc = 0.0f;
+  for (int64_t k0 = 0; k0 < K; k0 += 16) {
+    const int64_t ka = k0 + tx;
+    As[ty][tx] = (row < M && ka < K) ? load16<BF16>(A, row * K + ka) : 0.0f;
+    const int64_t kb = k0 + ty;
+    float bv = 0.0f;
+    if (kb < K && col < N) bv = b_kmajor ? load16<BF16>(B, col * K + kb) : load16<BF16>(B, kb * N + col);
+    Bs[ty][tx] = bv;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc = fmaf(As[ty][i], Bs[i][tx], acc);
+    __syncthreads();
+  }
+  if (row < M && col < N) {
+    float v = acc;
+    if (R != nullptr) v += load16<BF16>(R, row * N + col);
+    store16<BF16>(C, row * N + col, v);
+  }
+}
+
+}  // namespace
+
+int gemm_tc_general(const void* A, const void* B, const void* residual, void* C, int64_t M,
+                    int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
+                    cudaStream_t stream);
+
+int gemm_tc(const void* A, const void* B, const void* residual, void* C, int64_t M, int64_t N,
+            int64_t K, bool bf16, bool b_kmajor, cudaStream_t stream) {
+  return gemm_tc_general(A, B, residual, C, M, N, K, bf16, b_kmajor, false, 0, stream);
+}
+
+int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C, int64_t M,
+                     int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
+                     cudaStream_t stream);
+
+int gemm_tc_general(const void* A, const void* B, const void* residual, void* C, int64_t M,
+                    int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
+                    cudaStream_t stream) {
+  const int rc = gemm_tc_dispatch(A, B, residual, C, M, N, K, bf16, b_kmajor, hilo, half_b, stream);
+  if (rc != ENGINE_OK) return rc;
+  return check_launch("matmul/linear (tcgen05)");
+}
+
+/// With hilo=true, A holds 2*half_b activation rows (FP16 roundings, then the
+/// FP16 roundings of the remainders) of a batch padded to half_b rows, b_kmajor
+/// must be true, and the result rows are the first `M` rows of C.
+int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C, int64_t M,
+                    int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
+                    cudaStream_t stream) {
+  const CUtensorMapDataType dt =
+      bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(A), pb = reinterpret_cast<uintptr_t>(B);
+  const bool tma_ok = (K % 8 == 0) && (pa % 16 == 0) && (pb % 16 == 0) &&
+                      (b_kmajor || (N % 8 == 0));
+  if (!tma_ok) {
+    B200_REQUIRE(!hilo, "internal: hi/lo activations need 16-byte aligned rows");
+    dim3 grid(static_cast<unsigned>((N + 15) / 16), static_cast<unsigned>((M + 15) / 16));
+    B200_REQUIRE(grid.y <= 65535, "matmul: M too large for the fallback kernel");
+    if (bf16) {
+      gemm16_simt_kernel<true><<<grid, 256, 0, stream>>>(A, B, residual, C, M, N, K, b_kmajor);
+    } else {
+      gemm16_simt_kernel<false><<<grid, 256, 0, stream>>>(A, B, residual, C, M, N, K, b_kmajor);
+    }
+    return ENGINE_OK;
+  }
+
+  const int sms = sm_count();
+  TcParams p = {};
+  p.K = K;
+  p.num_kb = (K + kBK - 1) / kBK;
+  p.out = C;
+  p.resid = residual;
+  p.ldo = N;
+  p.out_rows = M;
+  p.out_cols = N;
+  p.err = device_error_word();
+  p.limit_ns = wait_limit_ns();
+  p.vec_out = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
+              (residual == nullptr || reinterpret_cast<uintptr_t>(residual) % 16 == 0);
+  const bool resid = residual != nullptr;
+
+  // Small batch against [N,K] weights: weights are the 128-row UMMA operand.
+  const int64_t act_rows = hilo ? 2 * static_cast<int64_t>(half_b) : M;
+  static const int swap_max = env_int("ENGINE_TC_SWAP_MAX_M", 64);
+  if (b_kmajor && act_rows <= 64 && (hilo || M <= swap_max)) {
+    int bn = 16;
+    while (bn < act_rows) bn <<= 1;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, B, dt, 2, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(K), kBM, kBK))
+      return ENGINE_ERR_UNSUPPORTED;
+    if (!make_tmap_2d(&tb, A, dt, 2, static_cast<uint64_t>(act_rows), static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(K), static_cast<uint32_t>(bn), kBK))
+      return ENGINE_ERR_UNSUPPORTED;
+    p.tiles_m = static_cast<int>((N + kBM - 1) / kBM);
+    p.tiles_n = 1;
+    p.half_b = half_b;
+    const int tiles = p.tiles_m;
+    int S = 1;
+    if (tiles < sms) {
+      S = sms / tiles;
+      if (S > 8) S = 8;
+      const int64_t kmax = p.num_kb / 4;  // at least four k-blocks per split
+      if (S > kmax) S = static_cast<int>(kmax > 0 ? kmax : 1);
+    }
+    static const int split_env = env_int("ENGINE_TC_SPLIT", 0);
+    if (split_env > 0) S = split_env > 8 ? 8 : split_env;
+    p.split = S;
+    p.kb_per_split = (p.num_kb + S - 1) / S;
+    const int grid = tiles;
+    if (hilo) {
+      switch (bn) {
+        case 16: return bf16 ? launch_tc_r<16, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<16, false, true, true, false>(resid, ta, tb, p, grid, stream);
+        case 32: return bf16 ? launch_tc_r<32, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<32, false, true, true, false>(resid, ta, tb, p, grid, stream);
+        default: return bf16 ? launch_tc_r<64, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, true, true, false>(resid, ta, tb, p, grid, stream);
+      }
+    }
+    switch (bn) {
+      case 16: return bf16 ? launch_tc_r<16, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<16, false, true, false, false>(resid, ta, tb, p, grid, stream);
+      case 32: return bf16 ? launch_tc_r<32, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<32, false, true, false, false>(resid, ta, tb, p, grid, stream);
+      default: return bf16 ? launch_tc_r<64, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, true, false, false>(resid, ta, tb, p, grid, stream);
+    }
+  }
+  B200_REQUIRE(!hilo, "internal: hi/lo activations are limited to 32 rows");
+
+  // General persistent GEMM: 128 x BN output tiles.
+  static const int bn_env = env_int("ENGINE_TC_BN", 0);
+  int bn = bn_env > 0 ? bn_env : (N >= 256 ? 256 : (N > 64 ? 128 : 64));
+  if (bn != 64 && bn != 128 && bn != 256) bn = 256;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, dt, 2, static_cast<uint64_t>(M), static_cast<uint64_t>(K),
+                    static_cast<uint64_t>(K), kBM, kBK))
+    return ENGINE_ERR_UNSUPPORTED;
+  if (b_kmajor) {
+    if (!make_tmap_2d(&tb, B, dt, 2, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(K), static_cast<uint32_t>(bn), kBK))
+      return ENGINE_ERR_UNSUPPORTED;
+  } else {
+    // B[K,N]: 64-wide (128-byte) column boxes, 64 k-rows each.
+    if (!make_tmap_2d(&tb, B, dt, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                      static_cast<uint64_t>(N), kBK, 64))
+      return ENGINE_ERR_UNSUPPORTED;
+  }
+  p.tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  p.tiles_n = static_cast<int>((N + bn - 1) / bn);
+  p.split = 1;
+  p.kb_per_split = p.num_kb;
+  p.half_b = 0;
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  if (b_kmajor) {
+    switch (bn) {
+      case 64: return bf16 ? launch_tc_r<64, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, false, false, false>(resid, ta, tb, p, grid, stream);
+      case 128: return bf16 ? launch_tc_r<128, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<128, false, false, false, false>(resid, ta, tb, p, grid, stream);
+      default: return bf16 ? launch_tc_r<256, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<256, false, false, false, false>(resid, ta, tb, p, grid, stream);
+    }
+  }
+  switch (bn) {
+    case 64: return bf16 ? launch_tc_r<64, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, true, false, false, false>(resid, ta, tb, p, grid, stream);
+    case 128: return bf16 ? launch_tc_r<128, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<128, true, false, false, false>(resid, ta, tb, p, grid, stream);
+    default: return bf16 ? launch_tc_r<256, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<256, true, false, false, false>(resid, ta, tb, p, grid, stream);
+  }
+}
+
+}  // namespace b200

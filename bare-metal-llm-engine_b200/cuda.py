@@ -1,0 +1,87 @@
+"""Raw-pointer mirror of ``engine::cuda`` (include/engine/kernels.hpp:34-204).
+
+Same names, argument order and meaning as the reference's C++ launchers:
+device pointers are ints (``tensor.data_ptr()``), dimensions are int64 and the
+stream is last (an int handle, 0 = legacy default stream).  Every function
+raises :class:`EngineError` when the library rejects the call.
+"""
+from __future__ import annotations
+
+from . import _check, lib
+
+
+def _s(stream) -> int | None:
+    return int(stream) if stream else None
+
+
+def matmul_naive(A, B, C, M, N, K, stream=0):  # kernels.hpp:67
+    _check(lib().engine_cuda_matmul_naive(A, B, C, M, N, K, _s(stream)))
+
+
+def matmul_tiled(A, B, C, M, N, K, stream=0):  # kernels.hpp:74
+    _check(lib().engine_cuda_matmul_tiled(A, B, C, M, N, K, _s(stream)))
+
+
+def matmul_register_tiled(A, B, C, M, N, K, stream=0):  # kernels.hpp:80
+    _check(lib().engine_cuda_matmul_register_tiled(A, B, C, M, N, K, _s(stream)))
+
+
+def gemv(A, x, out, N, K, stream=0):  # kernels.hpp:85
+    _check(lib().engine_cuda_gemv(A, x, out, N, K, _s(stream)))
+
+
+def gemv_fp16(A, x, out, N, K, stream=0):  # kernels.hpp:120
+    _check(lib().engine_cuda_gemv_fp16(A, x, out, N, K, _s(stream)))
+
+
+def rmsnorm(inp, weight, out, rows, cols, eps, stream=0):  # kernels.hpp:62
+    _check(lib().engine_cuda_rmsnorm(inp, weight, out, rows, cols, eps, _s(stream)))
+
+
+def rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, stream=0):  # kernels.hpp:97
+    _check(lib().engine_cuda_rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, _s(stream)))
+
+
+def rmsnorm_linear_fused_direct(inp, rms_weight, W, out, M, N, K, eps, stream=0):  # kernels.hpp:102
+    _check(lib().engine_cuda_rmsnorm_linear_fused_direct(inp, rms_weight, W, out, M, N, K, eps,
+                                                         _s(stream)))
+
+
+def vector_add(a, b, out, n, stream=0):  # kernels.hpp:49
+    _check(lib().engine_cuda_vector_add(a, b, out, n, _s(stream)))
+
+
+def swiglu_fp16(gate, up, out, n, stream=0):  # kernels.hpp:141
+    _check(lib().engine_cuda_swiglu_f16(gate, up, out, n, _s(stream)))
+
+
+def embedding_fp16(table, ids, out, num_tokens, hidden_dim, vocab_size, stream=0):  # kernels.hpp:128
+    _check(lib().engine_cuda_embedding_f16(table, ids, out, num_tokens, hidden_dim, vocab_size,
+                                           _s(stream)))
+
+
+# -- new entry points for the B200 configurations ([N,K] weights, FP16/BF16) --
+
+def matmul_f16(A, B, C, M, N, K, stream=0):
+    _check(lib().engine_cuda_matmul_f16(A, B, C, M, N, K, _s(stream)))
+
+
+def matmul_bf16(A, B, C, M, N, K, stream=0):
+    _check(lib().engine_cuda_matmul_bf16(A, B, C, M, N, K, _s(stream)))
+
+
+def linear_f16(X, W, residual, Y, M, N, K, stream=0):
+    _check(lib().engine_cuda_linear_f16(X, W, residual, Y, M, N, K, _s(stream)))
+
+
+def linear_bf16(X, W, residual, Y, M, N, K, stream=0):
+    _check(lib().engine_cuda_linear_bf16(X, W, residual, Y, M, N, K, _s(stream)))
+
+
+def gemv_f16_nk(W, x, residual, y, N, K, stream=0):
+    _check(lib().engine_cuda_gemv_f16_nk(W, x, residual, y, N, K, _s(stream)))
+
+
+def rmsnorm_linear_f16(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
+    _check(lib().engine_cuda_rmsnorm_linear_f16(x, gamma, W, residual, Y, M, N, K, eps,
+                                                _s(stream)))

@@ -1,0 +1,118 @@
+"""Torch-tensor front end of the hot path.
+
+Tensors supply device memory and the current CUDA stream; every computation is
+a call into libengine_b200.so.  Inputs must be contiguous CUDA tensors of the
+stated dtype (checked here, loudly); outputs are allocated when not given.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import cuda as _c
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _req(t: torch.Tensor, dtype: torch.dtype, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the library has no CPU path)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous (row-major)")
+    return t
+
+
+def _ptr(t):
+    return 0 if t is None else t.data_ptr()
+
+
+def matmul_f32(A, B, out=None, variant: str = "register_tiled"):
+    """C = A @ B, FP32 [M,K] x [K,N] (engine::cuda::matmul_<variant>)."""
+    _req(A, torch.float32, "A")
+    _req(B, torch.float32, "B")
+    M, K = A.shape
+    N = B.shape[1]
+    C = out if out is not None else torch.empty(M, N, device=A.device, dtype=torch.float32)
+    fn = {"naive": _c.matmul_naive, "tiled": _c.matmul_tiled,
+          "register_tiled": _c.matmul_register_tiled}[variant]
+    fn(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, _stream())
+    return C
+
+
+def matmul(A, B, out=None):
+    """C = A @ B with FP16 or BF16 A[M,K], B[K,N] on tcgen05 tensor cores."""
+    bf16 = A.dtype == torch.bfloat16
+    dt = torch.bfloat16 if bf16 else torch.float16
+    _req(A, dt, "A")
+    _req(B, dt, "B")
+    M, K = A.shape
+    N = B.shape[1]
+    C = out if out is not None else torch.empty(M, N, device=A.device, dtype=dt)
+    (_c.matmul_bf16 if bf16 else _c.matmul_f16)(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K,
+                                                _stream())
+    return C
+
+
+def linear(X, W, residual=None, out=None):
+    """Y = X @ W^T (+ residual) with W stored [N,K]; FP16 or BF16."""
+    bf16 = X.dtype == torch.bfloat16
+    dt = torch.bfloat16 if bf16 else torch.float16
+    _req(X, dt, "X")
+    _req(W, dt, "W")
+    if residual is not None:
+        _req(residual, dt, "residual")
+    M, K = X.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty(M, N, device=X.device, dtype=dt)
+    (_c.linear_bf16 if bf16 else _c.linear_f16)(X.data_ptr(), W.data_ptr(), _ptr(residual),
+                                                Y.data_ptr(), M, N, K, _stream())
+    return Y
+
+
+def gemv(W, x, residual=None, out=None):
+    """y = W[N,K] @ x[K] (+ residual), FP16 decode GEMV."""
+    _req(W, torch.float16, "W")
+    _req(x, torch.float16, "x")
+    N, K = W.shape
+    y = out if out is not None else torch.empty(N, device=W.device, dtype=torch.float16)
+    _c.gemv_f16_nk(W.data_ptr(), x.data_ptr(), _ptr(residual), y.data_ptr(), N, K, _stream())
+    return y
+
+
+def rmsnorm_linear(x, gamma, W, eps: float = 1e-5, residual=None, out=None):
+    """Y = rmsnorm(x; gamma, eps) @ W^T (+ residual), FP16, W stored [N,K]."""
+    _req(x, torch.float16, "x")
+    _req(W, torch.float16, "W")
+    if gamma is not None:
+        _req(gamma, torch.float16, "gamma")
+    if residual is not None:
+        _req(residual, torch.float16, "residual")
+    M, K = x.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty(M, N, device=x.device, dtype=torch.float16)
+    _c.rmsnorm_linear_f16(x.data_ptr(), _ptr(gamma), W.data_ptr(), _ptr(residual), Y.data_ptr(),
+                          M, N, K, eps, _stream())
+    return Y
+
+
+def swiglu(gate, up, out=None):
+    _req(gate, torch.float16, "gate")
+    _req(up, torch.float16, "up")
+    o = out if out is not None else torch.empty_like(gate)
+    _c.swiglu_fp16(gate.data_ptr(), up.data_ptr(), o.data_ptr(), gate.numel(), _stream())
+    return o
+
+
+def embedding(table, ids, out=None):
+    _req(table, torch.float16, "table")
+    _req(ids, torch.int32, "ids")
+    V, D = table.shape
+    T = ids.numel()
+    o = out if out is not None else torch.empty(T, D, device=table.device, dtype=torch.float16)
+    _c.embedding_fp16(table.data_ptr(), ids.data_ptr(), o.data_ptr(), T, D, V, _stream())
+    return o

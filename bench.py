@@ -1,0 +1,450 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 matrix-multiply hot path (one JSON line on rank 0).
+
+Headline workload (BASELINE metric "FP16 GEMM TFLOP/s (4096^3) & GEMV HBM GB/s
+(4096x14336); % of B200 peak"):
+
+* step  = one FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] on tcgen05
+  (engine_cuda_matmul_f16), A, B ~ N(0,1), FP32 accumulate.  Operands rotate over
+  a pool of sets larger than the 126 MB L2, so every step starts cold.
+  ``value`` = whole-job TFLOP/s over the K timed steps (sum over ranks of the work
+  / max over ranks of the CUDA-event time).
+* ``gemv`` = the decode GEMV y[4096] = W[4096,14336] x (engine_cuda_gemv_f16_nk),
+  W ~ N(0,0.02), x ~ N(0,1), over a rotating pool of weight matrices (448 MiB),
+  reported in HBM GB/s of algorithmic bytes.
+* ``e2e`` = the GEMM metric through the C ABI with pinned HOST buffers: each step
+  copies A and B host->device, runs the GEMM and reads C back.
+* ``cpu_baseline`` = the reference engine's own cpu::matmul (oracle/_ref) on a
+  bounded row sample of the same GEMM, all host cores, rank 0 at N=1 only.
+
+``--impl reference`` times the reference's CPU implementation alone (the
+reference has no GPU path for this configuration) and prints its line.
+``--workload tp-decode|tp-prefill`` runs the Llama-3-8B-shaped tensor-parallel
+projection layer set instead (see bare-metal-llm-engine_b200/tp.py).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "bare-metal-llm-engine_b200"
+METRIC = "FP16 GEMM TFLOP/s (4096³) & GEMV HBM GB/s (4096×14336); % of B200 peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_pkg():
+    if "bmle_b200" in sys.modules:
+        return sys.modules["bmle_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "bmle_b200", PKG_DIR / "__init__.py", submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["bmle_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def traffic_for(kernel: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(kernel)
+    return None if v is None else float(v.get("bytes_per_launch", v) if isinstance(v, dict) else v)
+
+
+# --------------------------------------------------------------- clock sampling
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during the timed region."""
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = device_index
+            if vis:
+                try:
+                    idx = int(vis.split(",")[device_index])
+                except ValueError:
+                    idx = device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no clocks rather than fail
+            self._h = None
+
+    def _sample(self):
+        nv = self._nv
+        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except AttributeError:
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.samples.append(mhz)
+        self.reasons |= int(r) & ~0x1  # idle is not a slowdown
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if self._h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": [n for b, n in _REASONS.items() if self.reasons & b]}
+
+
+# --------------------------------------------------------------- CPU baseline
+
+def _oracle():
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import oracle
+
+    return oracle
+
+
+def cpu_gemm_sample(A32, B32, rows: int, nthreads: int):
+    """Times the reference's cpu::matmul (oracle/_ref) -- else the oracle port --
+    on `rows` rows of the GEMM.  Returns (seconds, kind)."""
+    orc = _oracle()
+    sub = np.ascontiguousarray(A32[:rows])
+    M, K = sub.shape
+    N = B32.shape[1]
+    C = np.empty((M, N), np.float32)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if orc.ref_available():
+        t0 = time.perf_counter()
+        orc.ref_lib().ref_matmul(p(sub), p(B32), p(C), M, N, K, nthreads)
+        return time.perf_counter() - t0, "reference"
+    t0 = time.perf_counter()
+    orc.lib().orc_matmul_mt(p(sub), p(B32), p(C), M, N, K, nthreads)
+    return time.perf_counter() - t0, "port"
+
+
+def cpu_gemm_throughput(target_s: float, nthreads: int, n: int = 4096):
+    rng = np.random.default_rng(20260826)
+    A32 = rng.standard_normal((max(nthreads * 64, 64), n)).astype(np.float16).astype(np.float32)
+    B32 = rng.standard_normal((n, n)).astype(np.float16).astype(np.float32)
+    rows = nthreads
+    t, kind = cpu_gemm_sample(A32, B32, rows, nthreads)
+    while t < target_s * 0.5 and rows < A32.shape[0]:
+        rows = min(A32.shape[0], int(rows * max(2.0, target_s / max(t, 1e-3))))
+        rows = max(nthreads, rows - rows % nthreads)
+        t, kind = cpu_gemm_sample(A32, B32, rows, nthreads)
+    flops = 2.0 * rows * n * n
+    return flops / t / 1e12, kind, rows, t
+
+
+# --------------------------------------------------------------- distributed
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    world, rank, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return 0
+    orc = _oracle()
+    nthreads = orc.ncores()
+    n = 4096
+    rng = np.random.default_rng(20260826)
+    A32 = rng.standard_normal((nthreads * 8, n)).astype(np.float16).astype(np.float32)
+    B32 = rng.standard_normal((n, n)).astype(np.float16).astype(np.float32)
+    # size one step to ~0.5 s of CPU work
+    rows = nthreads
+    t, kind = cpu_gemm_sample(A32, B32, rows, nthreads)
+    while t < 0.25 and rows < A32.shape[0]:
+        rows = min(A32.shape[0], rows * 2)
+        t, kind = cpu_gemm_sample(A32, B32, rows, nthreads)
+    for _ in range(args.warmup):
+        cpu_gemm_sample(A32, B32, rows, nthreads)
+    times = []
+    for _ in range(args.steps):
+        dt, kind = cpu_gemm_sample(A32, B32, rows, nthreads)
+        times.append(dt)
+    total = sum(times)
+    flops = 2.0 * rows * n * n * args.steps
+    value = flops / total / 1e12
+    sample = (f"{rows} of 4096 output rows of the 4096^3 GEMM per step "
+              f"(engine::cpu::matmul, FP16 inputs widened to float)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (fp64 accumulate)", "data": "synthetic",
+        "config": {"workload": "FP16 GEMM 4096x4096x4096 (reference CPU oracle, row sample)",
+                   "M": n, "N": n, "K": n},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nthreads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- headline (ours)
+
+def time_launches(torch, fn, sets, steps, warmup, stream):
+    """Runs fn(set) warmup + steps times on rotating sets; returns per-launch and total ms."""
+    for i in range(warmup):
+        fn(sets[i % len(sets)])
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        ev[i][0].record(stream)
+        fn(sets[i % len(sets)])
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    per = [a.elapsed_time(b) for a, b in ev]
+    return per, t0.elapsed_time(t1)
+
+
+def run_headline(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    pkg = load_pkg()
+    pk, pk_kind = peaks()
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    n = 4096
+    g = torch.Generator(device=dev).manual_seed(20260826 + rank)
+
+    # ---- GEMM 4096^3 on a rotating pool (4 x 96 MiB > 126 MB L2)
+    nsets = 4
+    sets = []
+    for _ in range(nsets):
+        A = torch.randn(n, n, device=dev, generator=g).half()
+        B = torch.randn(n, n, device=dev, generator=g).half()
+        C = torch.empty(n, n, device=dev, dtype=torch.float16)
+        sets.append((A, B, C))
+    gemm = lambda s: pkg.cuda.matmul_f16(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                                         n, n, n, sp)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        per, total_ms = time_launches(torch, gemm, sets, args.steps, args.warmup, stream)
+    barrier(world)
+    flops = 2.0 * n * n * n
+    total_ms_max = max_over_ranks(total_ms, world)
+    value = world * flops * args.steps / (total_ms_max * 1e-3) / 1e12
+    gemm_kernel_ms = statistics.mean(per)
+    achieved = flops / (gemm_kernel_ms * 1e-3) / 1e12
+    peak_t = pk["bf16_tflops"]
+    del sets
+    torch.cuda.empty_cache()
+
+    # ---- decode GEMV y = W[4096,14336] x over 4 rotating weight matrices (448 MiB)
+    Nv, Kv = 4096, 14336
+    wsets = []
+    for _ in range(4):
+        W = (torch.randn(Nv, Kv, device=dev, generator=g) * 0.02).half()
+        x = torch.randn(Kv, device=dev, generator=g).half()
+        y = torch.empty(Nv, device=dev, dtype=torch.float16)
+        wsets.append((W, x, y))
+    gemv = lambda s: pkg.cuda.gemv_f16_nk(s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(),  # noqa: E731
+                                          Nv, Kv, sp)
+    gsteps = max(args.steps, 50)
+    barrier(world)
+    gper, gtotal = time_launches(torch, gemv, wsets, gsteps, max(args.warmup, 3), stream)
+    gbytes = 2.0 * (Nv * Kv + Kv + Nv)
+    gtotal_max = max_over_ranks(gtotal, world)
+    gemv_kernel_ms = statistics.mean(gper)
+    gemv_gbs = gbytes / (gemv_kernel_ms * 1e-3) / 1e9
+    gemv_job = world * gbytes * gsteps / (gtotal_max * 1e-3) / 1e9
+    del wsets
+    torch.cuda.empty_cache()
+
+    # ---- e2e through the C ABI with pinned host buffers
+    hA = torch.randn(n, n, generator=torch.Generator().manual_seed(1)).half().pin_memory()
+    hB = torch.randn(n, n, generator=torch.Generator().manual_seed(2)).half().pin_memory()
+    hC = torch.empty(n, n, dtype=torch.float16).pin_memory()
+    dA = torch.empty(n, n, device=dev, dtype=torch.float16)
+    dB = torch.empty_like(dA)
+    dC = torch.empty_like(dA)
+    esteps = max(3, min(args.steps, 50))
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        pkg.cuda.matmul_f16(dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), n, n, n, sp)
+        hC.copy_(dC, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(esteps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = world * flops * esteps / (e2e_ms * 1e-3) / 1e12
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        orc = _oracle()
+        nth = orc.ncores()
+        v, kind, rows, t = cpu_gemm_throughput(args.cpu_seconds, nth)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": nth, "kind": kind,
+               "sample": f"{rows} of 4096 output rows of the 4096^3 GEMM "
+                         f"({'engine::cpu::matmul' if kind == 'reference' else 'oracle port'}, "
+                         f"FP16 inputs widened to float), {t:.1f} s"}
+
+    traffic = traffic_for("gemm_tc_4096")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: seeded N(0,1) FP16 operands (torch Philox), W ~ N(0,0.02)",
+        "config": {"workload": "FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] "
+                               "(tcgen05, FP32 accumulate) + decode GEMV W[4096,14336] x",
+                   "M": n, "N": n, "K": n, "parallelism": f"replicas x{world}",
+                   "l2": "rotating operand pools larger than the 126 MB L2 "
+                         "(4 x 96 MiB GEMM sets, 4 x 112 MiB GEMV weights)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": achieved / peak_t, "traffic": traffic,
+                     "peak_kind": f"{pk_kind} bf16 dense burst",
+                     "kernel": "gemm_tc_kernel 4096^3", "kernel_ms": gemm_kernel_ms},
+        "gemv": {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / pk["hbm_gbs"],
+                 "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
+                 "kernel_us": gemv_kernel_ms * 1e3, "job_gbs": gemv_job,
+                 "bytes_per_launch": gbytes, "traffic": traffic_for("gemv_nk_4096x14336")},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["headline", "tp-decode", "tp-prefill"], default="headline")
+    ap.add_argument("--batch", type=int, default=1, help="tp-decode batch (1 or 32)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload != "headline":
+        tp = importlib.import_module("bmle_b200.tp") if "bmle_b200" in sys.modules else None
+        load_pkg()
+        from bmle_b200 import tp  # noqa: F811
+
+        return tp.bench_main(args, METRIC)
+    return run_headline(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,135 @@
+#pragma once
+//===----------------------------------------------------------------------===//
+// engine/kernels_b200.hpp -- the engine's C++ launch API over the B200 C ABI.
+//
+// Restores the exact signatures of include/engine/kernels.hpp (namespace
+// engine::cuda, raw device pointers, int64 dims, `cudaStream_t stream = 0`) on
+// top of include/engine_b200.h, so an engine translation unit switches to the
+// B200 kernels by including this header instead of kernels.hpp and linking
+// libengine_b200.so in place of kernels/matmul*.cu, gemv*.cu and
+// rmsnorm_linear.cu.  A nonzero status is rethrown as engine::EngineError with
+// the library's message, like the reference's ENGINE_CHECK (check.hpp:36-65).
+//
+// When the engine's own <engine/check.hpp> is reachable its EngineError is
+// used, so existing catch sites and EXPECT_THROWS_MSG checks keep working;
+// otherwise a compatible engine::EngineError is declared here.
+//===----------------------------------------------------------------------===//
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "../engine_b200.h"
+
+#if __has_include(<engine/check.hpp>) && __has_include(<engine/config.hpp>)
+#include <engine/check.hpp>
+#else
+namespace engine {
+class EngineError : public std::runtime_error {
+ public:
+  explicit EngineError(const std::string& what) : std::runtime_error(what) {}
+};
+}  // namespace engine
+#endif
+
+namespace engine::cuda {
+
+namespace b200_detail {
+inline void check(int rc) {
+  if (rc != ENGINE_OK) throw ::engine::EngineError(std::string("[engine] ") + engine_last_error());
+}
+inline const engine_half_t* h(const __half* p) { return reinterpret_cast<const engine_half_t*>(p); }
+inline engine_half_t* h(__half* p) { return reinterpret_cast<engine_half_t*>(p); }
+}  // namespace b200_detail
+
+// -- kernels.hpp:62-104, 120: the legacy hot-path launchers ------------------
+
+inline void rmsnorm(const float* in, const float* weight, float* out, std::int64_t rows,
+                    std::int64_t cols, float eps, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_rmsnorm(in, weight, out, rows, cols, eps, stream));
+}
+
+inline void matmul_naive(const float* A, const float* B, float* C, std::int64_t M,
+                         std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_matmul_naive(A, B, C, M, N, K, stream));
+}
+
+inline void matmul_tiled(const float* A, const float* B, float* C, std::int64_t M,
+                         std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_matmul_tiled(A, B, C, M, N, K, stream));
+}
+
+inline void matmul_register_tiled(const float* A, const float* B, float* C, std::int64_t M,
+                                  std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_matmul_register_tiled(A, B, C, M, N, K, stream));
+}
+
+inline void gemv(const float* A, const float* x, float* out, std::int64_t N, std::int64_t K,
+                 cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_gemv(A, x, out, N, K, stream));
+}
+
+inline void rmsnorm_linear(const float* in, const float* rms_weight, const float* W, float* out,
+                           std::int64_t M, std::int64_t N, std::int64_t K, float eps,
+                           cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_rmsnorm_linear(in, rms_weight, W, out, M, N, K, eps, stream));
+}
+
+inline void rmsnorm_linear_fused_direct(const float* in, const float* rms_weight, const float* W,
+                                        float* out, std::int64_t M, std::int64_t N,
+                                        std::int64_t K, float eps, cudaStream_t stream = 0) {
+  b200_detail::check(
+      engine_cuda_rmsnorm_linear_fused_direct(in, rms_weight, W, out, M, N, K, eps, stream));
+}
+
+inline void gemv_fp16(const __half* A, const __half* x, __half* out, std::int64_t N,
+                      std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_gemv_fp16(b200_detail::h(A), b200_detail::h(x),
+                                           b200_detail::h(out), N, K, stream));
+}
+
+inline void vector_add(const float* a, const float* b, float* out, std::int64_t n,
+                       cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_vector_add(a, b, out, n, stream));
+}
+
+inline void swiglu_fp16(const __half* gate, const __half* up, __half* out, std::int64_t n,
+                        cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_swiglu_f16(b200_detail::h(gate), b200_detail::h(up),
+                                            b200_detail::h(out), n, stream));
+}
+
+// -- new B200 entry points: FP16/BF16 and [N,K] weights ------------------------
+
+inline void matmul_f16(const __half* A, const __half* B, __half* C, std::int64_t M,
+                       std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_matmul_f16(b200_detail::h(A), b200_detail::h(B),
+                                            b200_detail::h(C), M, N, K, stream));
+}
+
+inline void linear_f16(const __half* X, const __half* W, const __half* residual, __half* Y,
+                       std::int64_t M, std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_linear_f16(b200_detail::h(X), b200_detail::h(W),
+                                            b200_detail::h(residual), b200_detail::h(Y), M, N, K,
+                                            stream));
+}
+
+inline void gemv_f16_nk(const __half* W, const __half* x, const __half* residual, __half* y,
+                        std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_gemv_f16_nk(b200_detail::h(W), b200_detail::h(x),
+                                             b200_detail::h(residual), b200_detail::h(y), N, K,
+                                             stream));
+}
+
+inline void rmsnorm_linear_f16(const __half* x, const __half* gamma, const __half* W,
+                               const __half* residual, __half* Y, std::int64_t M, std::int64_t N,
+                               std::int64_t K, float eps, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_rmsnorm_linear_f16(
+      b200_detail::h(x), b200_detail::h(gamma), b200_detail::h(W), b200_detail::h(residual),
+      b200_detail::h(Y), M, N, K, eps, stream));
+}
+
+}  // namespace engine::cuda

@@ -1,0 +1,170 @@
+/*
+ * engine_b200.h -- C ABI of the B200 (sm_100a) matrix-multiply hot path.
+ *
+ * Drop-in boundary for the launch API of Parag63/bare-metal-llm-engine
+ * (include/engine/kernels.hpp, namespace engine::cuda).  Each engine_cuda_<name>
+ * symbol below replaces the engine::cuda::<name> launcher cited beside it, with
+ * the same argument order and meaning: raw DEVICE pointers, int64 dimensions, all
+ * 2-D data row-major and contiguous, and the CUDA stream last (0 = legacy default
+ * stream).  include/engine/kernels_b200.hpp wraps these symbols back into the
+ * engine's C++ signatures and rethrows failures as engine::EngineError.
+ *
+ * Error convention (the reference's ENGINE_CHECK / CUDA_CHECK, check.hpp:36-107,
+ * expressed without C++ exceptions): every entry point returns ENGINE_OK (0) or a
+ * nonzero ENGINE_ERR_* code, and engine_last_error() returns the calling thread's
+ * message for its most recent failure.  Messages keep the reference's wording so
+ * substring checks carry over: "... must be non-negative" / "negative dimension",
+ * "... is null" / "null device pointer", "eps must be non-negative".
+ *
+ * Empty work follows the reference launchers: M == 0 or N == 0 returns ENGINE_OK
+ * without launching; K == 0 writes the zero matrix / vector (the empty sum)
+ * asynchronously on `stream` (matmul_register_tiled.cu:184-191, gemv_fp16.cu:124-131),
+ * except rmsnorm_linear, which like the reference returns without writing when any
+ * of M, N, K is zero (rmsnorm_linear.cu:180).
+ *
+ * All calls are asynchronous and stream-ordered.  They allocate no device memory
+ * of their own on the hot path: split-K partial sums are reduced through
+ * distributed shared memory inside a thread-block cluster.  They are safe to call
+ * from several host threads on different streams.
+ *
+ * FP16 / BF16 data crosses the ABI as 16-bit IEEE binary16 / bfloat16 bit
+ * patterns (engine::half is __half: the same 2-byte layout, half.hpp:28).
+ */
+#ifndef ENGINE_B200_H_
+#define ENGINE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ENGINE_B200_API __attribute__((visibility("default")))
+#else
+#define ENGINE_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* engine_stream_t; /* identical to cudaStream_t */
+typedef uint16_t engine_half_t;              /* IEEE binary16 bits (engine::half) */
+typedef uint16_t engine_bf16_t;              /* bfloat16 bits */
+
+enum {
+  ENGINE_OK = 0,
+  ENGINE_ERR_INVALID = 1,     /* bad argument: negative dim, null pointer, eps < 0 */
+  ENGINE_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+  ENGINE_ERR_UNSUPPORTED = 3, /* shape / alignment outside what the kernels support */
+  ENGINE_ERR_DEVICE = 4,      /* a kernel reported a device-side error (wait timeout) */
+  ENGINE_ERR_INTERNAL = 5
+};
+
+/* Version of this ABI (bumped on any signature change). */
+ENGINE_B200_API int engine_abi_version(void);
+
+/* Message of the calling thread's most recent failed call ("" if none). */
+ENGINE_B200_API const char* engine_last_error(void);
+
+/* Reads and clears the device-side error word of `device` (bits: 1 = a bounded
+ * wait inside a kernel ran out, 2 = a kernel's own bounds check fired).  Kernels
+ * set it instead of hanging; the call synchronises the device first. */
+ENGINE_B200_API int engine_device_status(int device, unsigned int* flags);
+
+/* ---------------------------------------------------------------------------
+ * Legacy launch API (FP32 and FP16 [K,N] layouts), kept behaviour-compatible.
+ * ------------------------------------------------------------------------- */
+
+/* C[M,N] = A[M,K] * B[K,N], FP32.  kernels.hpp:67 (matmul_naive). */
+ENGINE_B200_API int engine_cuda_matmul_naive(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                             int64_t K, engine_stream_t stream);
+/* kernels.hpp:74 (matmul_tiled). */
+ENGINE_B200_API int engine_cuda_matmul_tiled(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                             int64_t K, engine_stream_t stream);
+/* kernels.hpp:80 (matmul_register_tiled). */
+ENGINE_B200_API int engine_cuda_matmul_register_tiled(const float* A, const float* B, float* C, int64_t M,
+                                      int64_t N, int64_t K, engine_stream_t stream);
+
+/* out[N] = x[K] * A[K,N], FP32.  kernels.hpp:85 (gemv). */
+ENGINE_B200_API int engine_cuda_gemv(const float* A, const float* x, float* out, int64_t N, int64_t K,
+                     engine_stream_t stream);
+
+/* out[N] = x[K] * A[K,N], FP16 in/out, FP32 accumulate.  kernels.hpp:120 (gemv_fp16). */
+ENGINE_B200_API int engine_cuda_gemv_fp16(const engine_half_t* A, const engine_half_t* x, engine_half_t* out,
+                          int64_t N, int64_t K, engine_stream_t stream);
+
+/* Row RMSNorm, eps inside the square root; weight may be null.  kernels.hpp:62 (rmsnorm). */
+ENGINE_B200_API int engine_cuda_rmsnorm(const float* in, const float* weight, float* out, int64_t rows,
+                        int64_t cols, float eps, engine_stream_t stream);
+
+/* out[M,N] = rmsnorm(in[M,K], rms_weight, eps) * W[K,N]; rms_weight may be null.
+ * kernels.hpp:97 (rmsnorm_linear).  One fused launch for every M. */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear(const float* in, const float* rms_weight, const float* W,
+                               float* out, int64_t M, int64_t N, int64_t K, float eps,
+                               engine_stream_t stream);
+/* kernels.hpp:102 (rmsnorm_linear_fused_direct): same fused kernel. */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear_fused_direct(const float* in, const float* rms_weight,
+                                            const float* W, float* out, int64_t M, int64_t N,
+                                            int64_t K, float eps, engine_stream_t stream);
+
+/* out[i] = a[i] + b[i].  kernels.hpp:49 (vector_add): the residual add that the new
+ * entry points fold into their epilogues. */
+ENGINE_B200_API int engine_cuda_vector_add(const float* a, const float* b, float* out, int64_t n,
+                           engine_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * New entry points for the B200 configurations (tcgen05 / HBM-streaming).
+ * No reference counterpart exists for these layouts; each is the FP16/BF16,
+ * [N,K]-weight form of the legacy call named beside it.
+ * ------------------------------------------------------------------------- */
+
+/* C[M,N] = A[M,K] * B[K,N] (all row-major), FP16 in/out, FP32 accumulate, on
+ * tcgen05 tensor cores.  FP16 form of kernels.hpp:80 (matmul_register_tiled). */
+ENGINE_B200_API int engine_cuda_matmul_f16(const engine_half_t* A, const engine_half_t* B, engine_half_t* C,
+                           int64_t M, int64_t N, int64_t K, engine_stream_t stream);
+/* BF16 form of the above. */
+ENGINE_B200_API int engine_cuda_matmul_bf16(const engine_bf16_t* A, const engine_bf16_t* B, engine_bf16_t* C,
+                            int64_t M, int64_t N, int64_t K, engine_stream_t stream);
+
+/* Y[M,N] = X[M,K] * W[N,K]^T (+ residual[M,N] if non-null), FP16, FP32 accumulate:
+ * the activation x weight projection with weights stored [N,K] (K contiguous).
+ * M == 1 streams W through the decode GEMV; small M uses a swap-AB tcgen05 tile;
+ * larger M the persistent tcgen05 GEMM.  Residual form of matmul_register_tiled +
+ * vector_add (tests/test_kernels.cu:2805-2810). */
+ENGINE_B200_API int engine_cuda_linear_f16(const engine_half_t* X, const engine_half_t* W,
+                           const engine_half_t* residual, engine_half_t* Y, int64_t M,
+                           int64_t N, int64_t K, engine_stream_t stream);
+/* BF16 form of the above. */
+ENGINE_B200_API int engine_cuda_linear_bf16(const engine_bf16_t* X, const engine_bf16_t* W,
+                            const engine_bf16_t* residual, engine_bf16_t* Y, int64_t M,
+                            int64_t N, int64_t K, engine_stream_t stream);
+
+/* y[N] = W[N,K] * x[K] (+ residual[N]), FP16, FP32 accumulate: the batch-1 decode
+ * GEMV over [N,K] weights.  [N,K] form of kernels.hpp:120 (gemv_fp16). */
+ENGINE_B200_API int engine_cuda_gemv_f16_nk(const engine_half_t* W, const engine_half_t* x,
+                            const engine_half_t* residual, engine_half_t* y, int64_t N,
+                            int64_t K, engine_stream_t stream);
+
+/* Y[M,N] = rmsnorm(x[M,K], gamma, eps) * W[N,K]^T (+ residual), FP16 in/out, FP32
+ * accumulate, eps inside the square root, gamma may be null.  FP16 [N,K] form of
+ * kernels.hpp:97 (rmsnorm_linear). */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16(const engine_half_t* x, const engine_half_t* gamma,
+                                   const engine_half_t* W, const engine_half_t* residual,
+                                   engine_half_t* Y, int64_t M, int64_t N, int64_t K,
+                                   float eps, engine_stream_t stream);
+
+/* out[i] = silu(gate[i]) * up[i], FP16: glue between the gate/up and down
+ * projections of the tensor-parallel layer.  kernels.hpp:141 (swiglu_fp16). */
+ENGINE_B200_API int engine_cuda_swiglu_f16(const engine_half_t* gate, const engine_half_t* up,
+                           engine_half_t* out, int64_t n, engine_stream_t stream);
+
+/* out[t, :] = table[ids[t], :], FP16 rows: token-embedding glue of the layer set.
+ * kernels.hpp:128 (embedding_fp16); ids outside [0, vocab) are rejected on device
+ * by writing zeros and setting error bit 2. */
+ENGINE_B200_API int engine_cuda_embedding_f16(const engine_half_t* table, const int32_t* ids,
+                              engine_half_t* out, int64_t num_tokens, int64_t hidden,
+                              int64_t vocab, engine_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ENGINE_B200_H_ */

@@ -1,0 +1,161 @@
+"""CPU: the C-ABI library loads, exports every symbol include/engine_b200.h
+declares, and enforces the reference's argument contract.
+
+The contract tests mirror the reference's launchers_reject_negative_dimensions,
+launchers_reject_null_pointers and empty_work_is_a_no_op_not_an_error
+(tests/test_kernels.cu:1664-1838): argument validation happens before any
+device work, so they run without a GPU (the pointers are never dereferenced).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "engine_b200.h"
+P = 4096  # a non-null pointer value; never dereferenced by a rejected call
+
+
+def header_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"ENGINE_B200_API\s+(?:int|const char\*)\s+(engine_\w+)\(", text)))
+
+
+def test_header_declares_the_boundary():
+    syms = header_symbols()
+    for legacy in ["matmul_naive", "matmul_tiled", "matmul_register_tiled", "gemv", "gemv_fp16",
+                   "rmsnorm", "rmsnorm_linear", "rmsnorm_linear_fused_direct"]:
+        assert f"engine_cuda_{legacy}" in syms
+    assert len(syms) >= 20
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.lib()
+    out = subprocess.run(["nm", "-D", "--defined-only", str(pkg.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (engine_\w+)", out))
+    for s in header_symbols():
+        assert s in exported, f"{s} declared in engine_b200.h but not exported"
+        assert hasattr(lib, s)
+    assert set(pkg.EXPORTS) <= exported
+    assert lib.engine_abi_version() == 1
+
+
+def test_library_has_no_cuda_shared_object_dependency(pkg):
+    out = subprocess.run(["ldd", str(pkg.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcudart" not in out and "libcuda.so" not in out
+
+
+def _throws(pkg, fn, *args, substr):
+    with pytest.raises(pkg.EngineError) as e:
+        fn(*args)
+    assert substr in str(e.value), str(e.value)
+    assert e.value.code == 1
+
+
+def test_launchers_reject_negative_dimensions(pkg):
+    c = pkg.cuda
+    _throws(pkg, c.rmsnorm, P, P, P, -1, 4, 1e-5, substr="negative")
+    _throws(pkg, c.matmul_naive, P, P, P, -1, 4, 4, substr="negative")
+    _throws(pkg, c.matmul_tiled, P, P, P, 4, 4, -1, substr="negative")
+    _throws(pkg, c.rmsnorm_linear, P, P, P, P, -1, 4, 4, 1e-5, substr="negative")
+    _throws(pkg, c.rmsnorm_linear, P, P, P, P, 4, -1, 4, 1e-5, substr="negative")
+    _throws(pkg, c.rmsnorm_linear, P, P, P, P, 4, 4, -1, 1e-5, substr="negative")
+    _throws(pkg, c.gemv, P, P, P, -1, 4, substr="non-negative")
+    _throws(pkg, c.gemv, P, P, P, 4, -1, substr="non-negative")
+    _throws(pkg, c.gemv_fp16, P, P, P, -1, 4, substr="non-negative")
+    _throws(pkg, c.gemv_fp16, P, P, P, 4, -1, substr="non-negative")
+    _throws(pkg, c.matmul_register_tiled, P, P, P, -1, 4, 4, substr="non-negative")
+    _throws(pkg, c.matmul_register_tiled, P, P, P, 4, -1, 4, substr="non-negative")
+    _throws(pkg, c.matmul_register_tiled, P, P, P, 4, 4, -1, substr="non-negative")
+    _throws(pkg, c.vector_add, P, P, P, -1, substr="non-negative")
+    _throws(pkg, c.swiglu_fp16, P, P, P, -1, substr="non-negative")
+    _throws(pkg, c.matmul_f16, P, P, P, 4, 4, -1, substr="non-negative")
+    _throws(pkg, c.linear_f16, P, P, 0, P, -1, 4, 4, substr="non-negative")
+    _throws(pkg, c.gemv_f16_nk, P, P, 0, P, -1, 4, substr="non-negative")
+    _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, -1, 4, 1e-5, substr="negative")
+    # eps < 0 would put a negative number under the square root.
+    _throws(pkg, c.rmsnorm, P, P, P, 4, 4, -1.0, substr="eps")
+    _throws(pkg, c.rmsnorm_linear, P, P, P, P, 4, 4, 4, -1.0, substr="eps")
+    _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, 4, 4, -1.0, substr="eps")
+
+
+def test_launchers_reject_null_pointers(pkg):
+    c = pkg.cuda
+    _throws(pkg, c.rmsnorm, 0, P, P, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm, P, P, 0, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.matmul_naive, 0, P, P, 2, 2, 2, substr="null")
+    _throws(pkg, c.matmul_tiled, P, P, 0, 2, 2, 2, substr="null")
+    _throws(pkg, c.rmsnorm_linear, 0, P, P, P, 2, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm_linear, P, P, 0, P, 2, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm_linear, P, P, P, 0, 2, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.gemv, 0, P, P, 4, 4, substr="null")
+    _throws(pkg, c.gemv, P, 0, P, 4, 4, substr="null")
+    _throws(pkg, c.gemv, P, P, 0, 4, 4, substr="null")
+    _throws(pkg, c.gemv_fp16, 0, P, P, 4, 4, substr="null")
+    _throws(pkg, c.gemv_fp16, P, 0, P, 4, 4, substr="null")
+    _throws(pkg, c.gemv_fp16, P, P, 0, 4, 4, substr="null")
+    _throws(pkg, c.matmul_register_tiled, 0, P, P, 2, 2, 2, substr="null")
+    _throws(pkg, c.matmul_register_tiled, P, 0, P, 2, 2, 2, substr="null")
+    _throws(pkg, c.matmul_register_tiled, P, P, 0, 2, 2, 2, substr="null")
+    _throws(pkg, c.matmul_f16, P, 0, P, 2, 2, 2, substr="null")
+    _throws(pkg, c.linear_bf16, P, 0, 0, P, 2, 2, 2, substr="null")
+    _throws(pkg, c.rmsnorm_linear_f16, P, P, 0, 0, P, 2, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.swiglu_fp16, P, 0, P, 4, substr="null")
+    _throws(pkg, c.vector_add, P, P, 0, 4, substr="null")
+    # rms weight / gamma may be null: "no learned gain" is a valid configuration.
+    c.rmsnorm(P, 0, P, 0, 0, 1e-5)
+    c.rmsnorm_linear(P, 0, P, P, 0, 0, 0, 1e-5)
+    c.rmsnorm_linear_f16(P, 0, P, 0, P, 0, 0, 0, 1e-5)
+
+
+def test_empty_work_is_a_no_op_not_an_error(pkg):
+    c = pkg.cuda
+    c.rmsnorm(P, P, P, 0, 8, 1e-5)
+    c.rmsnorm(P, P, P, 8, 0, 1e-5)
+    c.matmul_naive(P, P, P, 0, 8, 8)
+    c.matmul_naive(P, P, P, 8, 0, 8)
+    c.matmul_tiled(P, P, P, 0, 8, 8)
+    c.matmul_tiled(P, P, P, 8, 0, 8)
+    c.matmul_register_tiled(P, P, P, 0, 8, 8)
+    c.matmul_register_tiled(P, P, P, 8, 0, 8)
+    c.rmsnorm_linear(P, P, P, P, 0, 8, 8, 1e-5)
+    c.rmsnorm_linear(P, P, P, P, 8, 0, 8, 1e-5)
+    c.rmsnorm_linear(P, P, P, P, 8, 8, 0, 1e-5)
+    c.gemv(P, P, P, 0, 8)
+    c.gemv_fp16(P, P, P, 0, 8)
+    c.swiglu_fp16(P, P, P, 0)
+    c.matmul_f16(P, P, P, 0, 8, 8)
+    c.linear_f16(P, P, 0, P, 8, 0, 8)
+    c.rmsnorm_linear_f16(P, P, P, 0, P, 8, 8, 0, 1e-5)
+
+
+def test_last_error_is_per_thread(pkg):
+    import threading
+
+    c = pkg.cuda
+    msgs = {}
+
+    def worker(name, args):
+        try:
+            c.gemv(*args)
+        except pkg.EngineError as e:
+            msgs[name] = str(e)
+
+    t1 = threading.Thread(target=worker, args=("a", (0, P, P, 4, 4)))
+    t2 = threading.Thread(target=worker, args=("b", (P, P, P, -1, 4)))
+    t1.start(); t2.start(); t1.join(); t2.join()
+    assert "null" in msgs["a"] and "non-negative" in msgs["b"]
+
+
+def test_cpp_adapter_header_compiles():
+    """include/engine/kernels_b200.hpp compiles as C++17 against the C ABI."""
+    src = '#include <engine/kernels_b200.hpp>\nint main(){return 0;}\n'
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", f"-I{ROOT / 'include'}",
+                        "-I/usr/local/cuda/include", "-x", "c++", "-"], input=src,
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
