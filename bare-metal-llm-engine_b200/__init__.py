@@ -108,4 +108,4 @@ def device_status(device: int = 0) -> int:
     return int(flags.value)
 
 
-from . import cuda, ops  # noqa: E402  (after lib/_check are defined)
+from . import cuda, ops, tp  # noqa: E402  (after lib/_check are defined)

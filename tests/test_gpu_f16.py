@@ -23,11 +23,25 @@ torch = pytest.importorskip("torch")
 EPS = 1e-5
 
 
+# Device copies made by dev_t stay alive until the test ends: the library is
+# handed raw pointers, so a temporary tensor must not be freed (and its memory
+# reused) before the call has run.
+_KEEP: list = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_device_tensors_alive():
+    yield
+    _KEEP.clear()
+
+
 def dev_t(a):
     a = np.ascontiguousarray(a)
     if a.dtype == np.uint16:  # bfloat16 bit patterns: move as int16
         a = a.view(np.int16)
-    return torch.from_numpy(a).cuda()
+    t = torch.from_numpy(a).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t):

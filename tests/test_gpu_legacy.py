@@ -20,11 +20,25 @@ K_MATMUL_RTOL, K_MATMUL_ATOL = 1e-4, 5e-5  # test_kernels.cu:171-172
 EPS = 1e-5
 
 
+# Device copies made by dev_t stay alive until the test ends: the library is
+# handed raw pointers, so a temporary tensor must not be freed (and its memory
+# reused) before the call has run.
+_KEEP: list = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_device_tensors_alive():
+    yield
+    _KEEP.clear()
+
+
 def dev_t(a, dtype=None):
     t = torch.from_numpy(np.ascontiguousarray(a))
     if dtype is not None:
         t = t.to(dtype)
-    return t.cuda()
+    t = t.cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t):

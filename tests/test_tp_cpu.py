@@ -1,0 +1,131 @@
+"""CPU: tensor-parallel sharding and collectives of the layer set on gloo ranks.
+
+World size 2 and 4 processes (spawned), a small Llama-shaped config, full
+weights drawn once from a seed and sharded with the product's own shard_layer /
+qkv_rows_for_rank / shard_head; projections by the float64 CPU test double.
+Every rank's TP result must equal the unsharded (t = 1) result, and the
+collective count must be exactly two all-reduces per layer.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests.conftest import load_package
+
+CFG_KW = dict(d_model=64, n_heads=8, n_kv_heads=4, head_dim=8, ffn=96, n_layers=3, vocab=200,
+              eps=1e-5)
+
+
+def full_weights(cfg, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "attn_norm": 1 + 0.1 * torch.randn(cfg.d_model, generator=g, dtype=torch.float64),
+            "ffn_norm": 1 + 0.1 * torch.randn(cfg.d_model, generator=g, dtype=torch.float64),
+            "qkv": 0.1 * torch.randn(cfg.qkv_rows, cfg.d_model, generator=g, dtype=torch.float64),
+            "o": 0.1 * torch.randn(cfg.d_model, cfg.n_heads * cfg.head_dim, generator=g, dtype=torch.float64),
+            "gate": 0.1 * torch.randn(cfg.ffn, cfg.d_model, generator=g, dtype=torch.float64),
+            "up": 0.1 * torch.randn(cfg.ffn, cfg.d_model, generator=g, dtype=torch.float64),
+            "down": 0.1 * torch.randn(cfg.d_model, cfg.ffn, generator=g, dtype=torch.float64),
+        })
+    lm = 0.1 * torch.randn(cfg.vocab, cfg.d_model, generator=g, dtype=torch.float64)
+    embed = torch.randn(cfg.vocab, cfg.d_model, generator=g, dtype=torch.float64)
+    fnorm = 1 + 0.1 * torch.randn(cfg.d_model, generator=g, dtype=torch.float64)
+    return layers, lm, embed, fnorm
+
+
+def run_model(tp, cfg, world, rank, ops, group=None):
+    layers, lm, embed, fnorm = full_weights(cfg)
+    shards = [tp.shard_layer(L, cfg, world, rank) for L in layers]
+    m = tp.TPLayerSet(cfg, rank, world, shards, tp.shard_head(lm, cfg, world, rank), embed, fnorm,
+                      ops=ops, group=group)
+    ids = torch.tensor([0, 5, 199, 42], dtype=torch.int32)
+    x = m.hidden(ops.embedding(embed, ids))
+    nxt = m.greedy(m.logits_shard(x))
+    return x, nxt, m.allreduce_count
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pkg = load_package()
+        from tests.tp_cpu_ops import CpuOps
+
+        tp = pkg.tp
+        cfg = tp.TPConfig(**CFG_KW)
+        x, nxt, n_ar = run_model(tp, cfg, world, rank, CpuOps())
+        q.put((rank, x.numpy(), nxt.numpy(), n_ar))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_layer_set_matches_unsharded_on_gloo(world):
+    pkg = load_package()
+    from tests.tp_cpu_ops import CpuOps
+
+    tp = pkg.tp
+    cfg = tp.TPConfig(**CFG_KW)
+    x1, n1, ar1 = run_model(tp, cfg, 1, 0, CpuOps())
+    assert ar1 == 0
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, x, nxt, n_ar in results:
+        assert not isinstance(x, str), f"rank {rank} failed: {x}"
+        torch.testing.assert_close(torch.from_numpy(x), x1, rtol=1e-12, atol=1e-12)
+        assert (nxt == n1.numpy()).all()
+        assert n_ar == 2 * cfg.n_layers
+
+
+def test_qkv_shards_are_head_aligned_and_partition_the_rows():
+    tp = load_package().tp
+    cfg = tp.LLAMA3_8B
+    for t in (1, 2, 4, 8):
+        rows = torch.cat([tp.qkv_rows_for_rank(cfg, t, r) for r in range(t)])
+        assert rows.numel() == cfg.qkv_rows
+        assert torch.equal(rows.sort().values, torch.arange(cfg.qkv_rows))
+        r0 = tp.qkv_rows_for_rank(cfg, t, 0)
+        assert r0.numel() == cfg.qkv_rows // t
+        # q block of rank 0 is whole heads
+        assert (r0[: cfg.n_heads // t * cfg.head_dim] < cfg.n_heads * cfg.head_dim).all()
+
+
+def test_tp_rejects_indivisible_degree():
+    tp = load_package().tp
+    with pytest.raises(ValueError):
+        tp.LLAMA3_8B.check(3)
+
+
+def test_weight_and_flop_accounting():
+    tp = load_package().tp
+    cfg = tp.LLAMA3_8B
+    assert abs(tp.weight_bytes_per_rank(cfg, 1) - 15.01e9) / 15.01e9 < 0.01
+    assert tp.weight_bytes_per_rank(cfg, 8) * 8 == pytest.approx(tp.weight_bytes_per_rank(cfg, 1))
