@@ -1,14 +1,16 @@
 // gemv.cu -- HBM-streaming matrix-vector products.
 //
-// 1. gemv_nk_kernel: y[m, n] = sum_k X[m, k] * W[n, k] for a handful of rows of X
-//    (batch-1 and tiny-batch decode) over weights stored [N,K], K contiguous --
-//    the layout of the B200 decode configuration.  One warp owns RPW weight rows;
-//    each lane streams 16-byte (8 x FP16) chunks of those rows with
-//    L1::no_allocate loads, U chunks in flight per row, multiplies them with the
-//    matching chunks of X (L1-resident after the first warp) and reduces with warp
-//    shuffles.  No shared memory, no split-K: N=4096 already gives 1024 CTAs.
-//    Optional fused RMSNorm (the warp accumulates sum(x^2) in the same pass and
-//    applies the scale after the dot product) and residual epilogue.
+// 1. gemv_nk_vec_kernel: y[m, n] = sum_k X[m, k] * W[n, k] for up to four rows
+//    of X (batch-1 and tiny-batch decode) over weights stored [N,K], K
+//    contiguous -- the layout of the B200 decode configuration.  A group of SK
+//    warps owns RPW weight rows; each lane streams 16-byte (8 x FP16) chunks of
+//    those rows with L1::no_allocate loads, software-pipelined so 2*U chunks per
+//    row are in flight, multiplies them with the matching chunks of X
+//    (L1-resident after the first warp) and reduces with warp shuffles, then
+//    across the SK warps through shared memory.  SK is chosen so that about 8k
+//    warps stream W at once (N=4096 -> SK=2).  Optional fused RMSNorm (sum(x^2)
+//    is accumulated in the same pass, the scale applied after the dot product)
+//    and residual epilogue.
 // 2. gemv_kn_kernel: out[n] = sum_k x[k] * A[k, n] over the reference's legacy
 //    [K,N] layout (engine::cuda::gemv / gemv_fp16, kernels/gemv*.cu).  A warp
 //    covers 32 x 16 bytes of one row of A per k, eight warps split K inside the
@@ -18,6 +20,7 @@
 //    rmsnorm_linear_f16.
 #include <cooperative_groups.h>
 
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -30,7 +33,7 @@ namespace {
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
@@ -48,17 +51,29 @@ __device__ __forceinline__ void h8_to_f8(const uint4& v, float (&f)[8]) {
 
 // ---------------------------------------------------------------- [N,K] GEMV
 
-constexpr int kNkWarps = 4;
+constexpr int kNkWarps = 4;     // scalar fallback: one row per warp
+constexpr int kNkVecWarps = 8;  // vector kernel: 8 warps per CTA
 
-template <int MR, int RPW, int U, bool NORM, bool RESID>
-__global__ void __launch_bounds__(kNkWarps * 32) gemv_nk_vec_kernel(
+// SK warps share one group of RPW weight rows: lane l of warp `sub` streams the
+// 16-byte chunks c = sub*32 + l + i*32*SK of every row, so the SK warps of a
+// group read 512*SK contiguous bytes per step.  Loads are software-pipelined
+// (two register buffers of U chunks per row: the next U chunks are in flight
+// while the current ones are multiplied).  Partial sums are reduced with warp
+// shuffles, then across the SK warps in fixed order through shared memory.
+template <int MR, int RPW, int SK, int U, bool NORM, bool RESID>
+__global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
     const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
     const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps) {
+  constexpr int GROUPS = kNkVecWarps / SK;
+  constexpr int NACC = MR * RPW + (NORM ? MR : 0);
+  __shared__ float red[kNkVecWarps][NACC];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kNkWarps + warp) * RPW;
-  if (row0 >= N) return;
+  const int grp = warp / SK;
+  const int sub = warp % SK;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * GROUPS + grp) * RPW;
   const int64_t nchunk = K >> 3;  // 8 halves per 16-byte chunk
+  constexpr int64_t kStride = 32 * SK;
 
   float acc[MR][RPW];
   float ss[MR];
@@ -68,57 +83,70 @@ __global__ void __launch_bounds__(kNkWarps * 32) gemv_nk_vec_kernel(
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[m][r] = 0.0f;
   }
-  const __half* wrow[RPW];
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: duplicate rows are not stored
-    wrow[r] = W + n * K;
-  }
 
-  for (int64_t c0 = lane; c0 < nchunk; c0 += 32 * U) {
-    uint4 wv[U][RPW];
-    uint4 xv[U][MR];
-    uint4 gv[U];
+  if (row0 < N) {
+    const __half* wrow[RPW];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t c = c0 + 32 * u;
-      if (c < nchunk) {
+    for (int r = 0; r < RPW; ++r) {
+      const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: never stored
+      wrow[r] = W + n * K;
+    }
+    uint4 wa[U][RPW], xa[U][MR], ga[U];
+    uint4 wb[U][RPW], xb[U][MR], gb[U];
+    auto load = [&](int64_t c0, uint4 (&w)[U][RPW], uint4 (&x)[U][MR], uint4 (&g)[U]) {
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) wv[u][r] = ld_stream_v4(wrow[r] + 8 * c);
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + kStride * u;
+        if (c < nchunk) {
 #pragma unroll
-        for (int m = 0; m < MR; ++m) xv[u][m] = __ldg(reinterpret_cast<const uint4*>(X + m * K + 8 * c));
-        if constexpr (NORM) {
-          gv[u] = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma + 8 * c))
-                        : make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+          for (int r = 0; r < RPW; ++r) w[u][r] = ld_stream_v4(wrow[r] + 8 * c);
+#pragma unroll
+          for (int m = 0; m < MR; ++m)
+            x[u][m] = __ldg(reinterpret_cast<const uint4*>(X + m * K + 8 * c));
+          if constexpr (NORM) {
+            g[u] = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma + 8 * c))
+                         : make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+          }
         }
       }
-    }
+    };
+    auto compute = [&](int64_t c0, uint4 (&w)[U][RPW], uint4 (&x)[U][MR], uint4 (&g)[U]) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t c = c0 + 32 * u;
-      if (c < nchunk) {
-        float g[8];
-        if constexpr (NORM) h8_to_f8(gv[u], g);
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + kStride * u;
+        if (c < nchunk) {
+          float gf[8];
+          if constexpr (NORM) h8_to_f8(g[u], gf);
 #pragma unroll
-        for (int m = 0; m < MR; ++m) {
-          float xf[8];
-          h8_to_f8(xv[u][m], xf);
-          if constexpr (NORM) {
+          for (int m = 0; m < MR; ++m) {
+            float xf[8];
+            h8_to_f8(x[u][m], xf);
+            if constexpr (NORM) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              ss[m] = fmaf(xf[i], xf[i], ss[m]);
-              xf[i] *= g[i];
+              for (int i = 0; i < 8; ++i) {
+                ss[m] = fmaf(xf[i], xf[i], ss[m]);
+                xf[i] *= gf[i];
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+              float wf[8];
+              h8_to_f8(w[u][r], wf);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[m][r] = fmaf(xf[i], wf[i], acc[m][r]);
             }
           }
-#pragma unroll
-          for (int r = 0; r < RPW; ++r) {
-            float wf[8];
-            h8_to_f8(wv[u][r], wf);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[m][r] = fmaf(xf[i], wf[i], acc[m][r]);
-          }
         }
       }
+    };
+    int64_t c0 = sub * 32 + lane;
+    load(c0, wa, xa, ga);
+    for (; c0 < nchunk; c0 += 2 * kStride * U) {
+      const int64_t c1 = c0 + kStride * U;
+      load(c1, wb, xb, gb);
+      compute(c0, wa, xa, ga);
+      load(c1 + kStride * U, wa, xa, ga);
+      compute(c1, wb, xb, gb);
     }
   }
 
@@ -134,25 +162,160 @@ __global__ void __launch_bounds__(kNkWarps * 32) gemv_nk_vec_kernel(
       for (int o = 16; o > 0; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
     }
   }
-  if (lane < RPW * MR) {
-    // Lane l writes row r = l % RPW of batch row m = l / RPW.
+  if (lane == 0) {
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        if (lane == m * RPW + r && row0 + r < N) {
-          float v = acc[m][r];
-          if constexpr (NORM) {
-            const float scale = static_cast<float>(
-                1.0 / sqrt(static_cast<double>(ss[m]) / static_cast<double>(K) +
-                           static_cast<double>(eps)));
-            v = v * scale;
-          }
-          if constexpr (RESID) v = v + __half2float(R[m * N + row0 + r]);
-          Y[m * N + row0 + r] = __float2half_rn(v);
+      for (int r = 0; r < RPW; ++r) red[warp][m * RPW + r] = acc[m][r];
+      if constexpr (NORM) red[warp][MR * RPW + m] = ss[m];
+    }
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < GROUPS * MR * RPW; o += blockDim.x) {
+    const int g = o / (MR * RPW);
+    const int rem = o % (MR * RPW);
+    const int m = rem / RPW;
+    const int r = rem % RPW;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * GROUPS + g) * RPW + r;
+    if (row >= N) continue;
+    float v = 0.0f;
+#pragma unroll
+    for (int q = 0; q < SK; ++q) v += red[g * SK + q][m * RPW + r];
+    if constexpr (NORM) {
+      float s2 = 0.0f;
+#pragma unroll
+      for (int q = 0; q < SK; ++q) s2 += red[g * SK + q][MR * RPW + m];
+      v = v * static_cast<float>(1.0 / sqrt(static_cast<double>(s2) / static_cast<double>(K) +
+                                            static_cast<double>(eps)));
+    }
+    if constexpr (RESID) v = v + __half2float(R[m * N + row]);
+    Y[m * N + row] = __float2half_rn(v);
+  }
+}
+
+// Batch-1 fused RMSNorm -> GEMV.  Each CTA first issues the loads of its first
+// weight chunks, then forms t = x * gamma (FP32) in shared memory and the sum of
+// squares of x with a block reduction -- once per CTA instead of once per warp
+// and chunk -- and streams W against t.  The RMS scale multiplies the finished
+// dot product: y = scale * sum_k t_k W_nk (+ residual).
+template <int RPW, int SK, int U, bool RESID>
+__global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
+    const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
+    const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps) {
+  constexpr int GROUPS = kNkVecWarps / SK;
+  extern __shared__ __align__(16) float s_t[];  // K floats
+  __shared__ float red[kNkVecWarps][RPW];
+  __shared__ float s_ss[kNkVecWarps];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int grp = warp / SK;
+  const int sub = warp % SK;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * GROUPS + grp) * RPW;
+  const int64_t nchunk = K >> 3;
+  constexpr int64_t kStride = 32 * SK;
+  const bool active = row0 < N;
+
+  const __half* wrow[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int64_t n = (row0 + r < N) ? row0 + r : N - 1;
+    wrow[r] = W + n * K;
+  }
+  uint4 wa[U][RPW], wb[U][RPW];
+  auto load = [&](int64_t c0, uint4 (&w)[U][RPW]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t c = c0 + kStride * u;
+      if (c < nchunk) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) w[u][r] = ld_stream_v4(wrow[r] + 8 * c);
+      }
+    }
+  };
+  int64_t c0 = sub * 32 + lane;
+  if (active) load(c0, wa);  // in flight while the prologue runs
+
+  // Prologue: t = x * gamma into shared memory, sum of squares of x.
+  float ss = 0.0f;
+  for (int64_t k8 = threadIdx.x; k8 < nchunk; k8 += blockDim.x) {
+    float xf[8], gf[8];
+    h8_to_f8(__ldg(reinterpret_cast<const uint4*>(X + 8 * k8)), xf);
+    if (gamma != nullptr) {
+      h8_to_f8(__ldg(reinterpret_cast<const uint4*>(gamma + 8 * k8)), gf);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gf[i] = 1.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(xf[i], xf[i], ss);
+      xf[i] *= gf[i];
+    }
+    float4* dst = reinterpret_cast<float4*>(s_t + 8 * k8);
+    dst[0] = make_float4(xf[0], xf[1], xf[2], xf[3]);
+    dst[1] = make_float4(xf[4], xf[5], xf[6], xf[7]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) s_ss[warp] = ss;
+  __syncthreads();
+
+  float acc[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+  auto compute = [&](int64_t cc, uint4 (&w)[U][RPW]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t c = cc + kStride * u;
+      if (c < nchunk) {
+        const float4 t0 = *reinterpret_cast<const float4*>(s_t + 8 * c);
+        const float4 t1 = *reinterpret_cast<const float4*>(s_t + 8 * c + 4);
+        const float tf[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          float wf[8];
+          h8_to_f8(w[u][r], wf);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[r] = fmaf(tf[i], wf[i], acc[r]);
         }
       }
     }
+  };
+  if (active) {
+    for (; c0 < nchunk; c0 += 2 * kStride * U) {
+      const int64_t c1 = c0 + kStride * U;
+      load(c1, wb);
+      compute(c0, wa);
+      load(c1 + kStride * U, wa);
+      compute(c1, wb);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) red[warp][r] = acc[r];
+  }
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNkVecWarps; ++w) total += s_ss[w];
+  const float scale = static_cast<float>(
+      1.0 / sqrt(static_cast<double>(total) / static_cast<double>(K) + static_cast<double>(eps)));
+  for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
+    const int g = o / RPW;
+    const int r = o % RPW;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * GROUPS + g) * RPW + r;
+    if (row >= N) continue;
+    float v = 0.0f;
+#pragma unroll
+    for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
+    v = v * scale;
+    if constexpr (RESID) v = v + __half2float(R[row]);
+    Y[row] = __float2half_rn(v);
   }
 }
 
@@ -197,36 +360,62 @@ int env_int(const char* name, int dflt) {
   return static_cast<int>(std::strtol(e, nullptr, 10));
 }
 
-template <int MR, int RPW, bool NORM, bool RESID>
+template <int MR, int RPW, int SK, bool NORM, bool RESID>
 void launch_nk_vec(const __half* W, const __half* X, const __half* gamma, const __half* R,
                    __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
-  constexpr int U = (MR >= 4) ? 2 : 4;
-  const int64_t rows_per_cta = static_cast<int64_t>(kNkWarps) * RPW;
+  constexpr int U = (MR >= 3) ? 2 : 4;
+  constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * RPW;
   const unsigned grid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
-  gemv_nk_vec_kernel<MR, RPW, U, NORM, RESID>
-      <<<grid, kNkWarps * 32, 0, stream>>>(W, X, gamma, R, Y, N, K, eps);
+  gemv_nk_vec_kernel<MR, RPW, SK, U, NORM, RESID>
+      <<<grid, kNkVecWarps * 32, 0, stream>>>(W, X, gamma, R, Y, N, K, eps);
 }
 
-template <int MR, bool NORM, bool RESID>
-void dispatch_rpw(int rpw, const __half* W, const __half* X, const __half* gamma,
-                  const __half* R, __half* Y, int64_t N, int64_t K, float eps,
-                  cudaStream_t stream) {
-  if (rpw >= 2) {
-    launch_nk_vec<MR, 2, NORM, RESID>(W, X, gamma, R, Y, N, K, eps, stream);
+template <int RPW, int SK, bool RESID>
+int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const __half* R,
+                    __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
+  constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * RPW;
+  const unsigned grid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
+  const size_t smem = static_cast<size_t>(K) * sizeof(float);
+  auto kern = gemv_nk_norm1_kernel<RPW, SK, 4, RESID>;
+  if (smem > 48 * 1024) {  // opt in once per device to the largest size the dispatch allows
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    B200_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = 1ull << (dev & 63);
+    if ((configured.load() & bit) == 0) {
+      B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(40960 * sizeof(float))));
+      configured.fetch_or(bit);
+    }
+  }
+  kern<<<grid, kNkVecWarps * 32, smem, stream>>>(W, X, gamma, R, Y, N, K, eps);
+  return ENGINE_OK;
+}
+
+template <int MR, int RPW, bool NORM, bool RESID>
+void dispatch_sk(int sk, const __half* W, const __half* X, const __half* gamma, const __half* R,
+                 __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
+  if (sk >= 4) {
+    launch_nk_vec<MR, RPW, 4, NORM, RESID>(W, X, gamma, R, Y, N, K, eps, stream);
+  } else if (sk == 2) {
+    launch_nk_vec<MR, RPW, 2, NORM, RESID>(W, X, gamma, R, Y, N, K, eps, stream);
   } else {
-    launch_nk_vec<MR, 1, NORM, RESID>(W, X, gamma, R, Y, N, K, eps, stream);
+    launch_nk_vec<MR, RPW, 1, NORM, RESID>(W, X, gamma, R, Y, N, K, eps, stream);
   }
 }
 
 template <bool NORM, bool RESID>
-void dispatch_mr(int64_t mr, int rpw, const __half* W, const __half* X, const __half* gamma,
-                 const __half* R, __half* Y, int64_t N, int64_t K, float eps,
+void dispatch_mr(int64_t mr, int rpw, int sk, const __half* W, const __half* X,
+                 const __half* gamma, const __half* R, __half* Y, int64_t N, int64_t K, float eps,
                  cudaStream_t stream) {
   switch (mr) {
-    case 1: dispatch_rpw<1, NORM, RESID>(rpw, W, X, gamma, R, Y, N, K, eps, stream); break;
-    case 2: dispatch_rpw<2, NORM, RESID>(rpw, W, X, gamma, R, Y, N, K, eps, stream); break;
-    case 3: dispatch_rpw<3, NORM, RESID>(rpw, W, X, gamma, R, Y, N, K, eps, stream); break;
-    default: dispatch_rpw<4, NORM, RESID>(rpw, W, X, gamma, R, Y, N, K, eps, stream); break;
+    case 1:
+      if (rpw >= 2) dispatch_sk<1, 2, NORM, RESID>(sk, W, X, gamma, R, Y, N, K, eps, stream);
+      else dispatch_sk<1, 1, NORM, RESID>(sk, W, X, gamma, R, Y, N, K, eps, stream);
+      break;
+    case 2: dispatch_sk<2, 1, NORM, RESID>(sk, W, X, gamma, R, Y, N, K, eps, stream); break;
+    case 3: dispatch_sk<3, 1, NORM, RESID>(sk, W, X, gamma, R, Y, N, K, eps, stream); break;
+    default: dispatch_sk<4, 1, NORM, RESID>(sk, W, X, gamma, R, Y, N, K, eps, stream); break;
   }
 }
 
@@ -437,19 +626,47 @@ int gemv_nk_f16(const __half* W, const __half* X, const __half* gamma, float eps
     }
     return check_launch("gemv_f16_nk");
   }
+  // Defaults from a sweep over the B200 decode shapes (CUDA-graph timing, cold
+  // L2): two weight rows per warp group; each row split over two warps unless K
+  // is long enough (> 8192) to keep one warp busy.  The fused-norm variant keeps
+  // one row per group (its per-chunk x-side work doubles the register load).
+  // ENGINE_GEMV_RPW / ENGINE_GEMV_SK override them for tuning sweeps.
   static const int rpw_env = env_int("ENGINE_GEMV_RPW", 0);
-  const int rpw = rpw_env > 0 ? rpw_env : (N >= 8192 ? 2 : 1);
+  static const int sk_env = env_int("ENGINE_GEMV_SK", 0);
+  const int rpw = rpw_env > 0 ? rpw_env : (norm ? 1 : 2);
+  int sk = sk_env > 0 ? sk_env : ((norm || K <= 8192) ? 2 : 1);
+  sk = sk >= 4 ? 4 : (sk >= 2 ? 2 : 1);
+  static const int norm1_env = env_int("ENGINE_GEMV_NORM1", 1);
+  if (norm && M == 1 && norm1_env != 0 && K <= 40960) {
+    // Batch-1 fused norm: x * gamma formed once per CTA in shared memory.
+    const int nsk = sk_env > 0 ? sk : 2;
+    const int nrpw = rpw_env > 0 ? rpw : 2;
+    int rc;
+    if (residual) {
+      rc = (nrpw >= 2) ? (nsk >= 2 ? launch_nk_norm1<2, 2, true>(W, X, gamma, residual, Y, N, K, eps, stream)
+                                   : launch_nk_norm1<2, 1, true>(W, X, gamma, residual, Y, N, K, eps, stream))
+                       : (nsk >= 2 ? launch_nk_norm1<1, 2, true>(W, X, gamma, residual, Y, N, K, eps, stream)
+                                   : launch_nk_norm1<1, 1, true>(W, X, gamma, residual, Y, N, K, eps, stream));
+    } else {
+      rc = (nrpw >= 2) ? (nsk >= 2 ? launch_nk_norm1<2, 2, false>(W, X, gamma, residual, Y, N, K, eps, stream)
+                                   : launch_nk_norm1<2, 1, false>(W, X, gamma, residual, Y, N, K, eps, stream))
+                       : (nsk >= 2 ? launch_nk_norm1<1, 2, false>(W, X, gamma, residual, Y, N, K, eps, stream)
+                                   : launch_nk_norm1<1, 1, false>(W, X, gamma, residual, Y, N, K, eps, stream));
+    }
+    if (rc != ENGINE_OK) return rc;
+    return check_launch("rmsnorm_linear_f16 (batch-1 GEMV)");
+  }
   for (int64_t m0 = 0; m0 < M; m0 += 4) {
     const int64_t mr = (M - m0 < 4) ? M - m0 : 4;
     const __half* Xm = X + m0 * K;
     const __half* Rm = residual ? residual + m0 * N : nullptr;
     __half* Ym = Y + m0 * N;
     if (norm) {
-      if (residual) dispatch_mr<true, true>(mr, rpw, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
-      else dispatch_mr<true, false>(mr, rpw, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
+      if (residual) dispatch_mr<true, true>(mr, rpw, sk, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
+      else dispatch_mr<true, false>(mr, rpw, sk, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
     } else {
-      if (residual) dispatch_mr<false, true>(mr, rpw, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
-      else dispatch_mr<false, false>(mr, rpw, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
+      if (residual) dispatch_mr<false, true>(mr, rpw, sk, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
+      else dispatch_mr<false, false>(mr, rpw, sk, W, Xm, gamma, Rm, Ym, N, K, eps, stream);
     }
   }
   return check_launch("gemv_f16_nk");

@@ -283,6 +283,68 @@ def time_launches(torch, fn, sets, steps, warmup, stream):
     return per, t0.elapsed_time(t1)
 
 
+def time_graph(torch, fn, sets, steps, warmup):
+    """Captures `steps` launches (rotating operand sets) in one CUDA graph and
+    times one replay with CUDA events on the replay stream; returns ms per launch.
+    Launch-bound kernels (~5-25 us) are timed without host enqueue gaps."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(warmup):
+            fn(sets[i % len(sets)], side.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for i in range(steps):
+            fn(sets[i % len(sets)], side.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    s = torch.cuda.current_stream()
+    e0.record(s)
+    g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    return ms
+
+
+def secondary_configs(torch, pkg, dev, g, world, args):
+    """The other BASELINE configurations, one line each (CUDA-graph timing,
+    operand pools larger than L2)."""
+    out = {}
+    # Config 3: fused RMSNorm -> QKV, W[6144,4096], B in {1, 16}
+    N, K = 6144, 4096
+    pool = [(torch.randn(16, K, device=dev, generator=g).half(),
+             (1 + 0.1 * torch.randn(K, device=dev, generator=g)).half(),
+             (torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+             torch.empty(16, N, device=dev, dtype=torch.float16)) for _ in range(5)]
+    for B in (1, 16):
+        fn = lambda s, st, B=B: pkg.cuda.rmsnorm_linear_f16(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0, s[3].data_ptr(), B, N, K, 1e-5, st)
+        ms = time_graph(torch, fn, pool, 100, 5)
+        byt = 2.0 * (N * K + B * K + K + B * N)
+        out[f"rmsnorm_qkv_b{B}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9}
+    del pool
+    # Config 4b: X[S,4096] W[14336,4096]^T
+    N, K = 14336, 4096
+    Ws = [(torch.randn(N, K, device=dev, generator=g) * 0.02).half() for _ in range(2)]
+    for S in (512, 2048, 4096):
+        X = torch.randn(S, K, device=dev, generator=g).half()
+        Y = torch.empty(S, N, device=dev, dtype=torch.float16)
+        sets = [(X, W, Y) for W in Ws]
+        fn = lambda s, st, S=S: pkg.cuda.linear_f16(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), S, N, K, st)
+        ms = time_graph(torch, fn, sets, 10 if S >= 2048 else 20, 3)
+        out[f"prefill_s{S}"] = {"us": ms * 1e3, "tflops": 2.0 * S * N * K / (ms * 1e-3) / 1e12}
+        del X, Y, sets
+    del Ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_headline(args):
     import torch
 
@@ -335,18 +397,18 @@ def run_headline(args):
         x = torch.randn(Kv, device=dev, generator=g).half()
         y = torch.empty(Nv, device=dev, dtype=torch.float16)
         wsets.append((W, x, y))
-    gemv = lambda s: pkg.cuda.gemv_f16_nk(s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(),  # noqa: E731
-                                          Nv, Kv, sp)
+    gemv = lambda s, st: pkg.cuda.gemv_f16_nk(s[0].data_ptr(), s[1].data_ptr(), 0,  # noqa: E731
+                                              s[2].data_ptr(), Nv, Kv, st)
     gsteps = max(args.steps, 50)
     barrier(world)
-    gper, gtotal = time_launches(torch, gemv, wsets, gsteps, max(args.warmup, 3), stream)
+    gemv_kernel_ms = max_over_ranks(time_graph(torch, gemv, wsets, gsteps, max(args.warmup, 3)), world)
     gbytes = 2.0 * (Nv * Kv + Kv + Nv)
-    gtotal_max = max_over_ranks(gtotal, world)
-    gemv_kernel_ms = statistics.mean(gper)
     gemv_gbs = gbytes / (gemv_kernel_ms * 1e-3) / 1e9
-    gemv_job = world * gbytes * gsteps / (gtotal_max * 1e-3) / 1e9
+    gemv_job = world * gemv_gbs
     del wsets
     torch.cuda.empty_cache()
+
+    secondary = secondary_configs(torch, pkg, dev, g, world, args) if not args.skip_secondary else None
 
     # ---- e2e through the C ABI with pinned host buffers
     hA = torch.randn(n, n, generator=torch.Generator().manual_seed(1)).half().pin_memory()
@@ -406,7 +468,9 @@ def run_headline(args):
         "gemv": {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / pk["hbm_gbs"],
                  "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
                  "kernel_us": gemv_kernel_ms * 1e3, "job_gbs": gemv_job,
-                 "bytes_per_launch": gbytes, "traffic": traffic_for("gemv_nk_4096x14336")},
+                 "bytes_per_launch": gbytes, "traffic": traffic_for("gemv_nk_4096x14336"),
+                 "timing": "CUDA graph of back-to-back launches, 4 x 112 MiB rotating weights"},
+        "other_configs": secondary,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2},
         "cpu_baseline": cpu,
@@ -432,6 +496,7 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=1, help="tp-decode batch (1 or 32)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-secondary", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

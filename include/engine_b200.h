@@ -22,10 +22,12 @@
  * except rmsnorm_linear, which like the reference returns without writing when any
  * of M, N, K is zero (rmsnorm_linear.cu:180).
  *
- * All calls are asynchronous and stream-ordered.  They allocate no device memory
- * of their own on the hot path: split-K partial sums are reduced through
- * distributed shared memory inside a thread-block cluster.  They are safe to call
- * from several host threads on different streams.
+ * All calls are asynchronous and stream-ordered and safe to call from several
+ * host threads on different streams.  Split-K partial sums are reduced through
+ * distributed shared memory inside a thread-block cluster, so the GEMM and GEMV
+ * paths need no scratch; the one exception is engine_cuda_rmsnorm_linear_f16
+ * with M > 4, whose normalised activation rows come from a library-owned
+ * stream-ordered memory pool.
  *
  * FP16 / BF16 data crosses the ABI as 16-bit IEEE binary16 / bfloat16 bit
  * patterns (engine::half is __half: the same 2-byte layout, half.hpp:28).
