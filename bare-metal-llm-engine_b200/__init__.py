@@ -55,6 +55,7 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_linear_bf16": [_p, _p, _p, _p, _i64, _i64, _i64, _p],
     "engine_cuda_gemv_f16_nk": [_p, _p, _p, _p, _i64, _i64, _p],
     "engine_cuda_rmsnorm_linear_f16": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
+    "engine_cuda_rmsnorm_linear_f16_noalloc": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_swiglu_f16": [_p, _p, _p, _i64, _p],
     "engine_cuda_embedding_f16": [_p, _p, _p, _i64, _i64, _i64, _p],
 }

@@ -45,6 +45,12 @@ int gemm_tc_general(const void* A, const void* B, const void* residual, void* C,
                     int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
                     cudaStream_t stream);
 
+/// Writes the hi/lo normalised activations of x[M,K] into out[2*hb, K] (rows
+/// [0,M) = FP16 roundings of (x*scale)*gamma, rows [hb, hb+M) = roundings of the
+/// remainders, all other rows zero).  linear.cu.
+int rmsnorm_hilo(const __half* x, const __half* gamma, __half* out, int64_t M, int64_t K, int hb,
+                 float eps, cudaStream_t stream);
+
 /// Stream-ordered scratch from the library's own per-device memory pool
 /// (cudaMallocFromPoolAsync; memory stays cached in the pool between calls).
 /// Returns nullptr with the error recorded on failure.  abi.cu.

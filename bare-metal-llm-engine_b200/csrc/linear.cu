@@ -75,6 +75,13 @@ int linear_impl(const void* X, const void* W, const void* R, void* Y, int64_t M,
 }
 
 }  // namespace
+
+int rmsnorm_hilo(const __half* x, const __half* gamma, __half* out, int64_t M, int64_t K, int hb,
+                 float eps, cudaStream_t stream) {
+  rmsnorm_hilo_kernel<<<hb, 256, 0, stream>>>(x, gamma, out, M, K, hb, eps);
+  return check_launch("rmsnorm_linear_f16 (normalise)");
+}
+
 }  // namespace b200
 
 using namespace b200;

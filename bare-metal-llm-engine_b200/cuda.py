@@ -85,3 +85,10 @@ def gemv_f16_nk(W, x, residual, y, N, K, stream=0):
 def rmsnorm_linear_f16(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
     _check(lib().engine_cuda_rmsnorm_linear_f16(x, gamma, W, residual, Y, M, N, K, eps,
                                                 _s(stream)))
+
+
+def rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
+    """rmsnorm_linear_f16 without any device allocation (fixed in-library scratch;
+    M <= 32, K <= 16384).  Concurrent calls on unordered streams race."""
+    _check(lib().engine_cuda_rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps,
+                                                        _s(stream)))

@@ -153,6 +153,22 @@ ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16(const engine_half_t* x, const
                                    engine_half_t* Y, int64_t M, int64_t N, int64_t K,
                                    float eps, engine_stream_t stream);
 
+/* rmsnorm_linear_f16 for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Same arguments and result as
+ * engine_cuda_rmsnorm_linear_f16, but the normalised activations live in a
+ * fixed 2 MiB array inside the library instead of a stream-ordered pool, so the
+ * call allocates nothing: for serving loops that reserve all device memory at
+ * start-up and may not allocate per request, and for hosts whose device memory
+ * is owned by another allocator.  Limits: 1 <= M <= 32, K <= 16384, K a multiple
+ * of 8, W 16-byte aligned; larger sizes return ENGINE_ERR_UNSUPPORTED.  The
+ * first call on each device looks up the array's device address; make it before
+ * any stream capture.  All calls share the one array: calls that overlap on the
+ * GPU race. */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16_noalloc(
+    const engine_half_t* x, const engine_half_t* gamma, const engine_half_t* W,
+    const engine_half_t* residual, engine_half_t* Y, int64_t M, int64_t N, int64_t K, float eps,
+    engine_stream_t stream);
+
 /* out[i] = silu(gate[i]) * up[i], FP16: glue between the gate/up and down
  * projections of the tensor-parallel layer.  kernels.hpp:141 (swiglu_fp16). */
 ENGINE_B200_API int engine_cuda_swiglu_f16(const engine_half_t* gate, const engine_half_t* up,
