@@ -44,6 +44,14 @@ bool always_sync_check() {
   return v;
 }
 
+bool pdl_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("ENGINE_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return v;
+}
+
 unsigned long long wait_limit_ns() {
   static const unsigned long long v = [] {
     const char* e = std::getenv("ENGINE_WAIT_TIMEOUT_MS");
@@ -259,6 +267,8 @@ __global__ void vector_add_kernel(const float* __restrict__ a, const float* __re
 // silu(g) * u in float with the library expf; FP16 out (round to nearest even).
 __global__ void swiglu_f16_kernel(const __half* __restrict__ g, const __half* __restrict__ u,
                                   __half* __restrict__ out, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float gv = __half2float(g[i]);
@@ -271,6 +281,8 @@ __global__ void swiglu_f16_kernel(const __half* __restrict__ g, const __half* __
 __global__ void embedding_f16_kernel(const __half* __restrict__ table,
                                      const int32_t* __restrict__ ids, __half* __restrict__ out,
                                      int64_t hidden, int64_t vocab, unsigned int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t t = blockIdx.x;
   const int32_t id = ids[t];
   const bool ok = id >= 0 && id < vocab;
@@ -354,9 +366,9 @@ int engine_cuda_swiglu_f16(const engine_half_t* gate, const engine_half_t* up,
   B200_REQUIRE(out != nullptr, "swiglu_fp16: out is null");
   B200_REQUIRE(n >= 0, "swiglu_fp16: n must be non-negative");
   if (n == 0) return ENGINE_OK;
-  swiglu_f16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(gate), reinterpret_cast<const __half*>(up),
-      reinterpret_cast<__half*>(out), n);
+  B200_CUDA(launch_pdl(swiglu_f16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, stream,
+                       reinterpret_cast<const __half*>(gate), reinterpret_cast<const __half*>(up),
+                       reinterpret_cast<__half*>(out), n));
   return check_launch("swiglu_fp16");
   B200_ENTRY_END
 }
@@ -372,9 +384,9 @@ int engine_cuda_embedding_f16(const engine_half_t* table, const int32_t* ids,
   B200_REQUIRE(vocab > 0, "embedding_fp16: vocab_size must be positive");
   if (num_tokens == 0 || hidden == 0) return ENGINE_OK;
   B200_REQUIRE(num_tokens <= 0x7fffffff, "embedding_fp16: too many tokens");
-  embedding_f16_kernel<<<static_cast<unsigned>(num_tokens), 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(table), ids, reinterpret_cast<__half*>(out), hidden,
-      vocab, device_error_word());
+  B200_CUDA(launch_pdl(embedding_f16_kernel, dim3(static_cast<unsigned>(num_tokens)), dim3(256), 0,
+                       stream, reinterpret_cast<const __half*>(table), ids,
+                       reinterpret_cast<__half*>(out), hidden, vocab, device_error_word()));
   return check_launch("embedding_fp16");
   B200_ENTRY_END
 }

@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/engine_b200.h"
 
@@ -49,6 +50,28 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled_fn();
+
+/// Programmatic dependent launch is on unless ENGINE_PDL=0.
+bool pdl_enabled();
+
+/// Launches `kern` with programmatic stream serialization (PDL): the kernel may
+/// start while its predecessor on the stream finishes, runs its set-up, and
+/// waits in griddepcontrol.wait before touching any input.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 /// 2-D row-major tensor map: `rows` x `cols` elements of `elem_bytes`, row pitch
 /// `ld` elements, box `box_rows` x `box_cols`, 128-byte swizzle.  Cached per
@@ -99,6 +122,15 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+// Programmatic dependent launch.  pdl_trigger lets the next kernel on the stream
+// begin launching (it still waits for this grid before reading anything);
+// pdl_wait blocks until the preceding grid has completed and its writes are
+// visible.  Both are no-ops when the launch did not enable PDL.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;

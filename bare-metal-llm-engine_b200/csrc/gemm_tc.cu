@@ -67,7 +67,24 @@ struct TcParams {
   int vec_out;           // 16-byte output stores allowed
   unsigned int* err;
   unsigned long long limit_ns;
+#ifdef ENGINE_TC_TRACE
+  unsigned long long* trace;  // debug builds: 8 timestamps per CTA
+#endif
 };
+
+#ifdef ENGINE_TC_TRACE
+#define TC_TRACE(slot)                                                                \
+  do {                                                                                \
+    if (p.trace) {                                                                    \
+      const uint32_t cta = blockIdx.x + gridDim.x * blockIdx.z;                        \
+      p.trace[cta * 8 + (slot)] = globaltimer();                                      \
+    }                                                                                 \
+  } while (0)
+#else
+#define TC_TRACE(slot) \
+  do {                 \
+  } while (0)
+#endif
 
 constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -75,13 +92,23 @@ constexpr int pow2_at_least(int v) {
   return p;
 }
 
-template <int BN>
+// SWAP (small-batch) tiles stream weights from HBM: their stage ring is kept under
+// ~113 KB so two CTAs fit per SM, which lets every split-K cluster of a launch be
+// resident at once (with one 190 KB CTA per SM, clusters of 3 leave SMs idle in
+// each GPC and spill into a second wave).
+template <int BN, bool SWAP = false>
 struct TcCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 10));
-  static constexpr int kTmemCols = pow2_at_least(2 * BN);
+  static constexpr int kStages =
+      SWAP ? (BN >= 64 ? 4 : (BN >= 32 ? 5 : 6))
+           : ((BN >= 256) ? 4 : (BN >= 128 ? 6 : (BN >= 64 ? 8 : 10)));
+  // Non-SWAP: two accumulators (double buffer across tiles).  SWAP (one tile per
+  // CTA): four accumulators that take k-blocks round-robin, so four independent
+  // MMA chains are in flight instead of one serial N=16..64 chain.
+  static constexpr int kAccs = SWAP ? 4 : 2;
+  static constexpr int kTmemCols = pow2_at_least(kAccs * BN);
   static constexpr int kPartialPitch = BN + 4;  // floats per row of the split-K partial
   static constexpr int kBarrierBytes = 256;
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
@@ -149,10 +176,10 @@ __device__ __forceinline__ void emit(const TcParams& p, int tm, int tn, int rl, 
 }
 
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const TcParams p) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, SWAP>;
   constexpr int ST = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -165,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) TC_TRACE(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -189,6 +217,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) TC_TRACE(1);
+  // Set-up done: let the next kernel start launching, then wait for the previous
+  // one (no operand or output is touched before this point).
+  pdl_trigger();
+  pdl_wait();
 
   const int64_t num_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   const int z = static_cast<int>(blockIdx.z);
@@ -218,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kABytes;
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          if (it == 0) TC_TRACE(2);
           tma_load_2d(sa, &tmA, &full[s], static_cast<int32_t>(kb * kBK), tm * kBM);
           if constexpr (B_MN) {
 #pragma unroll
@@ -231,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    __syncwarp();  // reconverge warp 0 before the CTA-wide barrier below
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -247,6 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t d_tmem = tmem_base + a * BN;
         for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
+          // SWAP: k-block i feeds accumulator i % 4 (first use overwrites).
+          const uint32_t i = static_cast<uint32_t>(kb - kb0);
+          const uint32_t d_acc = SWAP ? tmem_base + (i & 3u) * BN : d_tmem;
+          const bool first = SWAP ? (i < 4u) : (kb == kb0);
           const uint32_t s = it % ST;
           const uint32_t ph = (it / ST) & 1u;
           if (!mbar_wait(&full[s], ph, p.limit_ns, p.err)) {
@@ -254,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (it == 0) TC_TRACE(3);
           const uint32_t sa = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll
@@ -265,14 +305,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               bdesc = umma_desc_sw128(sb + kk * 32, 16, 1024);
             }
-            umma_f16(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            umma_f16(d_acc, adesc, bdesc, kIdesc, (!first || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
         if (!ok) break;
+        TC_TRACE(4);
         umma_commit(&tfull[a]);
       }
     }
+    __syncwarp();  // reconverge warp 1 (its lane 0 issued the MMAs)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -285,19 +327,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aph = (tl >> 1) & 1u;
       if (!mbar_wait(&tfull[a], aph, p.limit_ns, p.err)) break;
       tc_fence_after();
+      if (threadIdx.x == 64) TC_TRACE(5);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
+      // 16 accumulator columns [c, c+16) of this thread's row; in SWAP mode the sum
+      // of the accumulators that received k-blocks, in fixed order.
+      const int nacc = SWAP ? static_cast<int>((kb1 - kb0) < 4 ? (kb1 - kb0) : 4) : 1;
+      auto ld16 = [&](int c, float (&f)[16]) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(taddr + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(v[i]);
+        if constexpr (SWAP) {
+          for (int j = 1; j < nacc; ++j) {
+            tmem_ld_32x32b_x16(taddr + j * BN + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) f[i] += __uint_as_float(v[i]);
+          }
+        }
+      };
 
       if (p.split > 1) {
         // Park the FP32 partial in shared memory (the pipeline ring is idle now).
         float* P = reinterpret_cast<float*>(smem);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(taddr + c, v);
-          tmem_wait_ld();
+          float f[16];
+          ld16(c, f);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            P[rl * Cfg::kPartialPitch + c + i] = have_k ? __uint_as_float(v[i]) : 0.0f;
+          for (int i = 0; i < 16; ++i) P[rl * Cfg::kPartialPitch + c + i] = have_k ? f[i] : 0.0f;
         }
       } else if constexpr (SWAP) {
         if constexpr (HILO) {
@@ -306,11 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           float f[BN];
 #pragma unroll
           for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(taddr + c, v);
-            tmem_wait_ld();
+            float g16[16];
+            ld16(c, g16);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) f[c + i] = __uint_as_float(v[i]);
+            for (int i = 0; i < 16; ++i) f[c + i] = g16[i];
           }
 #pragma unroll
           for (int j = 0; j < BN / 2; ++j) {
@@ -319,12 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(taddr + c, v);
-            tmem_wait_ld();
+            float f[16];
+            ld16(c, f);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              emit<true, RESID, BF16>(p, tm, tn, rl, c + i, BN, __uint_as_float(v[i]));
+            for (int i = 0; i < 16; ++i) emit<true, RESID, BF16>(p, tm, tn, rl, c + i, BN, f[i]);
           }
         }
       } else {
@@ -384,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) TC_TRACE(6);
 
   if (p.split > 1) {
     // Sum the S partials of this tile in rank order; CTA z finishes rows z, z+S, ...
@@ -413,6 +470,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
+#ifdef ENGINE_TC_TRACE
+  if (threadIdx.x == 0 && p.trace) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    TC_TRACE(7);
+    p.trace[(blockIdx.x + gridDim.x * blockIdx.z) * 8 + 7] =
+        (p.trace[(blockIdx.x + gridDim.x * blockIdx.z) * 8 + 7] << 8) | smid;
+  }
+#endif
 }
 
 // ------------------------------------------------------------------ host side
@@ -420,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int grid_x,
               cudaStream_t stream) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, SWAP>;
   auto kern = gemm_tc_kernel<BN, B_MN, SWAP, HILO, RESID, BF16>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
@@ -431,19 +497,47 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, i
                                    Cfg::kSmemBytes));
     configured.fetch_or(bit);
   }
+  TcParams q = p;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(p.split));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = static_cast<unsigned>(p.split);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  if (q.split <= 0) {
+    // Automatic split-K (SWAP tiles): the largest cluster size S <= q.kb_per_split
+    // (the caller's cap) whose clusters are ALL co-resident, so no cluster waits
+    // for a second wave.  Occupancy per (device, S) is queried once and cached.
+    static std::atomic<int> fits[64][9];
+    const int cap = q.kb_per_split > 8 ? 8 : static_cast<int>(q.kb_per_split);
+    int best = 1;
+    for (int S = cap; S >= 2; --S) {
+      int n = fits[dev & 63][S].load();
+      if (n == 0) {
+        cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(S));
+        attr[0].val.clusterDim.z = static_cast<unsigned>(S);
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = -1;
+        cudaGetLastError();
+        fits[dev & 63][S].store(n == 0 ? -1 : n);
+      }
+      if (n >= grid_x) {
+        best = S;
+        break;
+      }
+    }
+    q.split = best;
+    q.kb_per_split = (q.num_kb + best - 1) / best;
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(q.split));
+  attr[0].val.clusterDim.z = static_cast<unsigned>(q.split);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, q));
   return ENGINE_OK;
 }
 
@@ -550,6 +644,12 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
   p.out_cols = N;
   p.err = device_error_word();
   p.limit_ns = wait_limit_ns();
+#ifdef ENGINE_TC_TRACE
+  {
+    const char* e = std::getenv("ENGINE_TC_TRACE_PTR");
+    p.trace = e ? reinterpret_cast<unsigned long long*>(std::strtoull(e, nullptr, 0)) : nullptr;
+  }
+#endif
   p.vec_out = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
               (residual == nullptr || reinterpret_cast<uintptr_t>(residual) % 16 == 0);
   const bool resid = residual != nullptr;
@@ -571,17 +671,28 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     p.tiles_n = 1;
     p.half_b = half_b;
     const int tiles = p.tiles_m;
-    int S = 1;
-    if (tiles < sms) {
-      S = sms / tiles;
-      if (S > 8) S = 8;
-      const int64_t kmax = p.num_kb / 4;  // at least four k-blocks per split
-      if (S > kmax) S = static_cast<int>(kmax > 0 ? kmax : 1);
+    // Split-K over a cluster when the weight tiles alone cannot cover the SMs
+    // (two CTAs fit per SM in this mode); launch_tc picks the cluster size from
+    // occupancy, capped here at 8 and at four k-blocks per split.
+    int cap = 1;
+    if (tiles < 2 * sms) {
+      cap = (2 * sms) / tiles;
+      if (cap > 8) cap = 8;
+      const int64_t kmax = p.num_kb / 4;
+      if (cap > kmax) cap = static_cast<int>(kmax > 0 ? kmax : 1);
+      if (cap < 1) cap = 1;
     }
     static const int split_env = env_int("ENGINE_TC_SPLIT", 0);
-    if (split_env > 0) S = split_env > 8 ? 8 : split_env;
-    p.split = S;
-    p.kb_per_split = (p.num_kb + S - 1) / S;
+    if (split_env > 0) {
+      p.split = split_env > 8 ? 8 : split_env;
+      p.kb_per_split = (p.num_kb + p.split - 1) / p.split;
+    } else if (cap > 1) {
+      p.split = 0;              // automatic
+      p.kb_per_split = cap;     // the cap, consumed by launch_tc
+    } else {
+      p.split = 1;
+      p.kb_per_split = p.num_kb;
+    }
     const int grid = tiles;
     if (hilo) {
       switch (bn) {

@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[m][r] = 0.0f;
   }
+  pdl_trigger();
+  pdl_wait();
 
   if (row0 < N) {
     const __half* wrow[RPW];
@@ -233,6 +235,8 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
     }
   };
   int64_t c0 = sub * 32 + lane;
+  pdl_trigger();
+  pdl_wait();
   if (active) load(c0, wa);  // in flight while the prologue runs
 
   // Prologue: t = x * gamma into shared memory, sum of squares of x.
@@ -366,8 +370,8 @@ void launch_nk_vec(const __half* W, const __half* X, const __half* gamma, const 
   constexpr int U = (MR >= 3) ? 2 : 4;
   constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * RPW;
   const unsigned grid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
-  gemv_nk_vec_kernel<MR, RPW, SK, U, NORM, RESID>
-      <<<grid, kNkVecWarps * 32, 0, stream>>>(W, X, gamma, R, Y, N, K, eps);
+  launch_pdl(gemv_nk_vec_kernel<MR, RPW, SK, U, NORM, RESID>, dim3(grid), dim3(kNkVecWarps * 32),
+             0, stream, W, X, gamma, R, Y, N, K, eps);
 }
 
 template <int RPW, int SK, bool RESID>
@@ -388,7 +392,8 @@ int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const
       configured.fetch_or(bit);
     }
   }
-  kern<<<grid, kNkVecWarps * 32, smem, stream>>>(W, X, gamma, R, Y, N, K, eps);
+  B200_CUDA(launch_pdl(kern, dim3(grid), dim3(kNkVecWarps * 32), smem, stream, W, X, gamma, R, Y,
+                       N, K, eps));
   return ENGINE_OK;
 }
 
