@@ -481,6 +481,250 @@ __global__ void __launch_bounds__(kThreads)
 #endif
 }
 
+// ------------------------------------------------------------ 2-SM (M = 256) GEMM
+//
+// A CTA pair (cluster of 2) computes a 256 x BN output tile with
+// tcgen05.mma.cta_group::2: CTA r holds rows [128r, 128r+128) of the A tile and
+// columns [r*BN/2, (r+1)*BN/2) of the B tile in its own shared memory, and rows
+// [128r, 128r+128) of the FP32 accumulator in its own TMEM.  Per SM this halves
+// the shared-memory operand bandwidth (and the L2 operand traffic) of a
+// 128 x BN tile.  Roles as in gemm_tc_kernel, with these cross-CTA links:
+//   * both producers wait on their own `empty` barrier, then load their halves;
+//     the leader (rank 0) arms its `full` barrier for BOTH CTAs' bytes and the
+//     peer's TMA completes on the leader's barrier (shared::cluster address);
+//   * the leader's MMA thread issues the 2-SM MMA and commits each stage (and
+//     each finished accumulator) to the barriers of BOTH CTAs -- two plain
+//     commits, one per CTA;
+//   * both epilogues drain their own TMEM lanes and arrive on the leader's
+//     `tempty` barrier (count 8 = 4 warps x 2 CTAs).
+// No TMA multicast is used.
+
+template <int BN>
+struct Tc2Cfg {
+  static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's BN/2 rows / columns of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN >= 256) ? 6 : 8;
+  static constexpr int kTmemCols = pow2_at_least(2 * BN);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+template <int BN, bool B_MN, bool RESID, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+  using Cfg = Tc2Cfg<BN>;
+  constexpr int ST = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+  uint64_t* empty = full + ST;
+  uint64_t* tfull = empty + ST;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 1);   // leader: its producer's expect_tx arrival
+      mbar_init(&empty[s], 1);  // one commit from the leader's MMA thread
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // leader: 4 epilogue warps x 2 CTAs
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  const int64_t num_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t npairs = gridDim.x >> 1;
+  const int64_t nkb = p.num_kb;
+  constexpr uint32_t kIdesc = umma_idesc_f16(256, BN, BF16, false, B_MN);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < num_tiles; t += npairs) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+          const uint32_t s = it % ST;
+          const uint32_t ph = (it / ST) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.limit_ns, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          const uint32_t fbar = full_leader0 + s * 8;
+          tma_load_2d_2sm(sa, &tmA, fbar, static_cast<int32_t>(kb * kBK),
+                          tm * 256 + static_cast<int>(rank) * 128);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) {
+              tma_load_2d_2sm(sb + j * 8192, &tmB, fbar,
+                              tn * BN + static_cast<int>(rank) * (BN / 2) + j * 64,
+                              static_cast<int32_t>(kb * kBK));
+            }
+          } else {
+            tma_load_2d_2sm(sb, &tmB, fbar, static_cast<int32_t>(kb * kBK),
+                            tn * BN + static_cast<int>(rank) * (BN / 2));
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t empty_self0 = mapa_shared(smem_u32(&empty[0]), 0);
+      const uint32_t tfull_peer0 = mapa_shared(smem_u32(&tfull[0]), 1);
+      const uint32_t tfull_self0 = mapa_shared(smem_u32(&tfull[0]), 0);
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < num_tiles; t += npairs, ++tl) {
+        const uint32_t a = tl & 1u;
+        const uint32_t aph = (tl >> 1) & 1u;
+        if (!mbar_wait(&tempty[a], aph ^ 1u, p.limit_ns, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+          const uint32_t s = it % ST;
+          const uint32_t ph = (it / ST) & 1u;
+          if (!mbar_wait(&full[s], ph, p.limit_ns, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = umma_desc_sw128(sa + kk * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_MN) {
+              bdesc = umma_desc_sw128(sb + kk * 2048, 8192, 1024);
+            } else {
+              bdesc = umma_desc_sw128(sb + kk * 32, 16, 1024);
+            }
+            umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_2sm(empty_self0 + s * 8);
+          umma_commit_2sm(empty_peer0 + s * 8);
+        }
+        if (!ok) break;
+        umma_commit_2sm(tfull_self0 + a * 8);
+        umma_commit_2sm(tfull_peer0 + a * 8);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int rl = q * 32 + lane;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    uint32_t tl = 0;
+    for (int64_t t = pair; t < num_tiles; t += npairs, ++tl) {
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const uint32_t a = tl & 1u;
+      const uint32_t aph = (tl >> 1) & 1u;
+      if (!mbar_wait(&tfull[a], aph, p.limit_ns, p.err)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
+      const int64_t row = static_cast<int64_t>(tm) * 256 + static_cast<int64_t>(rank) * 128 + rl;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + c, v);
+        tmem_wait_ld();
+        const int64_t col0 = static_cast<int64_t>(tn) * BN + c;
+        if (row < p.out_rows) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+          if (p.vec_out && col0 + 32 <= p.out_cols) {
+            const int64_t base = row * p.ldo + col0;
+            if constexpr (RESID) {
+              const uint4* rp = reinterpret_cast<const uint4*>(
+                  reinterpret_cast<const uint16_t*>(p.resid) + base);
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const uint4 rv = rp[g];
+                const uint16_t* rh = reinterpret_cast<const uint16_t*>(&rv);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float r;
+                  if constexpr (BF16) {
+                    r = __uint_as_float(static_cast<uint32_t>(rh[i]) << 16);
+                  } else {
+                    r = __half2float(__ushort_as_half(rh[i]));
+                  }
+                  f[g * 8 + i] += r;
+                }
+              }
+            }
+            uint4* op = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + base);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 o;
+              o.x = pack2<BF16>(f[g * 8 + 0], f[g * 8 + 1]);
+              o.y = pack2<BF16>(f[g * 8 + 2], f[g * 8 + 3]);
+              o.z = pack2<BF16>(f[g * 8 + 4], f[g * 8 + 5]);
+              o.w = pack2<BF16>(f[g * 8 + 6], f[g * 8 + 7]);
+              op[g] = o;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int64_t cc = col0 + i;
+              if (cc < p.out_cols) {
+                float vv = f[i];
+                if constexpr (RESID) vv += load16<BF16>(p.resid, row * p.ldo + cc);
+                store16<BF16>(p.out, row * p.ldo + cc, vv);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
@@ -538,6 +782,38 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, i
   attr[0].val.clusterDim.z = static_cast<unsigned>(q.split);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, q));
+  return ENGINE_OK;
+}
+
+template <int BN, bool B_MN, bool RESID, bool BF16>
+int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int grid_x,
+               cudaStream_t stream) {
+  using Cfg = Tc2Cfg<BN>;
+  auto kern = gemm_tc2_kernel<BN, B_MN, RESID, BF16>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((configured.load() & bit) == 0) {
+    B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg::kSmemBytes));
+    configured.fetch_or(bit);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
   return ENGINE_OK;
 }
 
@@ -708,6 +984,44 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     }
   }
   B200_REQUIRE(!hilo, "internal: hi/lo activations are limited to 32 rows");
+
+  // Large GEMMs: 2-SM tcgen05 (256 x BN tiles over CTA pairs).
+  static const int two_sm_env = env_int("ENGINE_TC_2SM", 1);
+  if (two_sm_env != 0 && M >= 256 && N >= 256) {
+    static const int bn2_env = env_int("ENGINE_TC2_BN", 0);
+    const int bn2 = (bn2_env == 128) ? 128 : 256;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, dt, 2, static_cast<uint64_t>(M), static_cast<uint64_t>(K),
+                      static_cast<uint64_t>(K), 128, kBK))
+      return ENGINE_ERR_UNSUPPORTED;
+    if (b_kmajor) {
+      if (!make_tmap_2d(&tb, B, dt, 2, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                        static_cast<uint64_t>(K), static_cast<uint32_t>(bn2 / 2), kBK))
+        return ENGINE_ERR_UNSUPPORTED;
+    } else {
+      if (!make_tmap_2d(&tb, B, dt, 2, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                        static_cast<uint64_t>(N), kBK, 64))
+        return ENGINE_ERR_UNSUPPORTED;
+    }
+    p.tiles_m = static_cast<int>((M + 255) / 256);
+    p.tiles_n = static_cast<int>((N + bn2 - 1) / bn2);
+    p.split = 1;
+    p.kb_per_split = p.num_kb;
+    p.half_b = 0;
+    const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+    const int pairs = static_cast<int>(tiles < sms / 2 ? tiles : sms / 2);
+    const int grid = 2 * pairs;
+    if (bn2 == 128) {
+      if (b_kmajor) return bf16 ? (resid ? launch_tc2<128, false, true, true>(ta, tb, p, grid, stream) : launch_tc2<128, false, false, true>(ta, tb, p, grid, stream))
+                                : (resid ? launch_tc2<128, false, true, false>(ta, tb, p, grid, stream) : launch_tc2<128, false, false, false>(ta, tb, p, grid, stream));
+      return bf16 ? (resid ? launch_tc2<128, true, true, true>(ta, tb, p, grid, stream) : launch_tc2<128, true, false, true>(ta, tb, p, grid, stream))
+                  : (resid ? launch_tc2<128, true, true, false>(ta, tb, p, grid, stream) : launch_tc2<128, true, false, false>(ta, tb, p, grid, stream));
+    }
+    if (b_kmajor) return bf16 ? (resid ? launch_tc2<256, false, true, true>(ta, tb, p, grid, stream) : launch_tc2<256, false, false, true>(ta, tb, p, grid, stream))
+                              : (resid ? launch_tc2<256, false, true, false>(ta, tb, p, grid, stream) : launch_tc2<256, false, false, false>(ta, tb, p, grid, stream));
+    return bf16 ? (resid ? launch_tc2<256, true, true, true>(ta, tb, p, grid, stream) : launch_tc2<256, true, false, true>(ta, tb, p, grid, stream))
+                : (resid ? launch_tc2<256, true, true, false>(ta, tb, p, grid, stream) : launch_tc2<256, true, false, false>(ta, tb, p, grid, stream));
+  }
 
   // General persistent GEMM: 128 x BN output tiles.
   static const int bn_env = env_int("ENGINE_TC_BN", 0);
