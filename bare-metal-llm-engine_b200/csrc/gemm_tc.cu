@@ -39,6 +39,7 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -51,6 +52,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 x 16-bit = 128 bytes: one 128B-swizzle row
 constexpr int kThreads = 192;
+constexpr int kEpiStageBytes = 128 * 64 * 2;  // one 128-row x 64-column 16-bit tile
 
 struct TcParams {
   int64_t K;
@@ -65,6 +67,7 @@ struct TcParams {
   int64_t out_cols;      // N of Y / C
   int half_b;            // HILO: columns [half_b, 2*half_b) hold the remainders
   int vec_out;           // 16-byte output stores allowed
+  int tma_epi;           // output written by TMA stores through shared memory
   unsigned int* err;
   unsigned long long limit_ns;
 #ifdef ENGINE_TC_TRACE
@@ -111,7 +114,8 @@ struct TcCfg {
   static constexpr int kTmemCols = pow2_at_least(kAccs * BN);
   static constexpr int kPartialPitch = BN + 4;  // floats per row of the split-K partial
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static constexpr int kEpiBytes = SWAP ? 0 : 2 * kEpiStageBytes;  // TMA-store staging
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
   static_assert(kStages * kStageBytes >= kBM * kPartialPitch * 4, "partial must fit");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -175,16 +179,57 @@ __device__ __forceinline__ void emit(const TcParams& p, int tm, int tn, int rl, 
   store16<BF16>(p.out, idx, v);
 }
 
+/// Epilogue through shared memory: the four epilogue warps (128 threads, one
+/// tile row each) convert 64 accumulator columns at a time into a 128-byte-
+/// swizzled 16 KB staging tile (conflict-free 16-byte writes), then one thread
+/// stores the tile with a TMA bulk-tensor store.  Two staging tiles alternate;
+/// `chunk` counts staged chunks across tiles.  TMA clips rows / columns
+/// outside the output, so edge tiles need no special case.
+template <int BN, bool BF16>
+__device__ __forceinline__ void epilogue_tma_tile(const CUtensorMap* tmC, uint8_t* stage,
+                                                  uint32_t taddr, int rl, bool elect,
+                                                  int32_t col_base, int32_t row0,
+                                                  uint32_t& chunk) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64, ++chunk) {
+    uint8_t* buf = stage + (chunk & 1u) * kEpiStageBytes;
+    if (elect) bulk_wait_group_read<1>();  // the store that last used `buf` has read it
+    named_barrier_sync(1, 128);
+    uint32_t v[2][32];
+    tmem_ld_32x32b_x32(taddr + c, v[0]);
+    tmem_ld_32x32b_x32(taddr + c + 32, v[1]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* w = &v[j >> 2][(j & 3) * 8];
+      uint4 o;
+      o.x = pack2<BF16>(__uint_as_float(w[0]), __uint_as_float(w[1]));
+      o.y = pack2<BF16>(__uint_as_float(w[2]), __uint_as_float(w[3]));
+      o.z = pack2<BF16>(__uint_as_float(w[4]), __uint_as_float(w[5]));
+      o.w = pack2<BF16>(__uint_as_float(w[6]), __uint_as_float(w[7]));
+      *reinterpret_cast<uint4*>(buf + rl * 128 + ((j ^ (rl & 7)) << 4)) = o;
+    }
+    fence_proxy_async_smem();
+    named_barrier_sync(1, 128);
+    if (elect) {
+      tma_store_2d(tmC, buf, col_base + c, row0);
+      bulk_commit_group();
+    }
+  }
+}
+
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
 __global__ void __launch_bounds__(kThreads)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                   const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const TcParams p) {
   using Cfg = TcCfg<BN, SWAP>;
   constexpr int ST = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+  uint8_t* epi_stage = smem + ST * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + ST;
   uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + 2;
@@ -320,6 +365,7 @@ __global__ void __launch_bounds__(kThreads)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int rl = q * 32 + lane;
     uint32_t tl = 0;
+    uint32_t epi_chunk = 0;
     for (int64_t t = t_begin; t < num_tiles; t += t_step, ++tl) {
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
@@ -383,6 +429,11 @@ __global__ void __launch_bounds__(kThreads)
             for (int i = 0; i < 16; ++i) emit<true, RESID, BF16>(p, tm, tn, rl, c + i, BN, f[i]);
           }
         }
+      } else if (!RESID && !SWAP && p.tma_epi) {
+        if constexpr (!RESID && !SWAP) {
+          epilogue_tma_tile<BN, BF16>(&tmC, epi_stage, taddr, rl, warp == 2 && lane == 0,
+                                      tn * BN, tm * kBM, epi_chunk);
+        }
       } else {
         const int64_t row = static_cast<int64_t>(tm) * kBM + rl;
 #pragma unroll 1
@@ -437,6 +488,7 @@ __global__ void __launch_bounds__(kThreads)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[a]);
     }
+    if (warp == 2 && lane == 0) bulk_wait_group<0>();  // TMA stores complete before exit
   }
 
   __syncthreads();
@@ -506,20 +558,23 @@ struct Tc2Cfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (BN >= 256) ? 6 : 8;
   static constexpr int kTmemCols = pow2_at_least(2 * BN);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 256 + 1024;
+  static constexpr int kEpiBytes = 2 * kEpiStageBytes;  // TMA-store staging
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 256 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 template <int BN, bool B_MN, bool RESID, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
   using Cfg = Tc2Cfg<BN>;
   constexpr int ST = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ST * Cfg::kStageBytes);
+  uint8_t* epi_stage = smem + ST * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + ST;
   uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + 2;
@@ -647,6 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int rl = q * 32 + lane;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     uint32_t tl = 0;
+    uint32_t epi_chunk = 0;
     for (int64_t t = pair; t < num_tiles; t += npairs, ++tl) {
       int tm, tn;
       tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
@@ -656,6 +712,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
       const int64_t row = static_cast<int64_t>(tm) * 256 + static_cast<int64_t>(rank) * 128 + rl;
+      if constexpr (!RESID) {
+        if (p.tma_epi) {
+          epilogue_tma_tile<BN, BF16>(&tmC, epi_stage, taddr, rl, warp == 2 && lane == 0,
+                                      tn * BN, tm * 256 + static_cast<int>(rank) * 128,
+                                      epi_chunk);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
@@ -714,6 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
     }
+    if (warp == 2 && lane == 0) bulk_wait_group<0>();  // TMA stores complete before exit
   }
 
   tc_fence_before();
@@ -728,8 +796,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ host side
 
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int grid_x,
-              cudaStream_t stream) {
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+              const TcParams& p, int grid_x, cudaStream_t stream) {
   using Cfg = TcCfg<BN, SWAP>;
   auto kern = gemm_tc_kernel<BN, B_MN, SWAP, HILO, RESID, BF16>;
   static std::atomic<uint64_t> configured{0};
@@ -781,13 +849,13 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, i
   cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(q.split));
   attr[0].val.clusterDim.z = static_cast<unsigned>(q.split);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, q));
+  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, q));
   return ENGINE_OK;
 }
 
 template <int BN, bool B_MN, bool RESID, bool BF16>
-int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, int grid_x,
-               cudaStream_t stream) {
+int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+               const TcParams& p, int grid_x, cudaStream_t stream) {
   using Cfg = Tc2Cfg<BN>;
   auto kern = gemm_tc2_kernel<BN, B_MN, RESID, BF16>;
   static std::atomic<uint64_t> configured{0};
@@ -813,15 +881,15 @@ int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  B200_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p));
   return ENGINE_OK;
 }
 
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool BF16>
-int launch_tc_r(bool resid, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
-                int grid_x, cudaStream_t stream) {
-  return resid ? launch_tc<BN, B_MN, SWAP, HILO, true, BF16>(ta, tb, p, grid_x, stream)
-               : launch_tc<BN, B_MN, SWAP, HILO, false, BF16>(ta, tb, p, grid_x, stream);
+int launch_tc_r(bool resid, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                const TcParams& p, int grid_x, cudaStream_t stream) {
+  return resid ? launch_tc<BN, B_MN, SWAP, HILO, true, BF16>(ta, tb, tc, p, grid_x, stream)
+               : launch_tc<BN, B_MN, SWAP, HILO, false, BF16>(ta, tb, tc, p, grid_x, stream);
 }
 
 int env_int(const char* name, int dflt) {
@@ -929,6 +997,17 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
   p.vec_out = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
               (residual == nullptr || reinterpret_cast<uintptr_t>(residual) % 16 == 0);
   const bool resid = residual != nullptr;
+  // Output tensor map for the TMA-store epilogue (general GEMM paths only).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  p.tma_epi = 0;
+  auto enable_tma_out = [&]() {
+    if (!resid && (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
+        make_tmap_2d(&tc, C, dt, 2, static_cast<uint64_t>(M), static_cast<uint64_t>(N),
+                     static_cast<uint64_t>(N), 128, 64)) {
+      p.tma_epi = 1;
+    }
+  };
 
   // Small batch against [N,K] weights: weights are the 128-row UMMA operand.
   const int64_t act_rows = hilo ? 2 * static_cast<int64_t>(half_b) : M;
@@ -972,15 +1051,15 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     const int grid = tiles;
     if (hilo) {
       switch (bn) {
-        case 16: return bf16 ? launch_tc_r<16, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<16, false, true, true, false>(resid, ta, tb, p, grid, stream);
-        case 32: return bf16 ? launch_tc_r<32, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<32, false, true, true, false>(resid, ta, tb, p, grid, stream);
-        default: return bf16 ? launch_tc_r<64, false, true, true, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, true, true, false>(resid, ta, tb, p, grid, stream);
+        case 16: return bf16 ? launch_tc_r<16, false, true, true, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<16, false, true, true, false>(resid, ta, tb, tc, p, grid, stream);
+        case 32: return bf16 ? launch_tc_r<32, false, true, true, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<32, false, true, true, false>(resid, ta, tb, tc, p, grid, stream);
+        default: return bf16 ? launch_tc_r<64, false, true, true, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<64, false, true, true, false>(resid, ta, tb, tc, p, grid, stream);
       }
     }
     switch (bn) {
-      case 16: return bf16 ? launch_tc_r<16, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<16, false, true, false, false>(resid, ta, tb, p, grid, stream);
-      case 32: return bf16 ? launch_tc_r<32, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<32, false, true, false, false>(resid, ta, tb, p, grid, stream);
-      default: return bf16 ? launch_tc_r<64, false, true, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, true, false, false>(resid, ta, tb, p, grid, stream);
+      case 16: return bf16 ? launch_tc_r<16, false, true, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<16, false, true, false, false>(resid, ta, tb, tc, p, grid, stream);
+      case 32: return bf16 ? launch_tc_r<32, false, true, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<32, false, true, false, false>(resid, ta, tb, tc, p, grid, stream);
+      default: return bf16 ? launch_tc_r<64, false, true, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<64, false, true, false, false>(resid, ta, tb, tc, p, grid, stream);
     }
   }
   B200_REQUIRE(!hilo, "internal: hi/lo activations are limited to 32 rows");
@@ -1003,6 +1082,7 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
                         static_cast<uint64_t>(N), kBK, 64))
         return ENGINE_ERR_UNSUPPORTED;
     }
+    enable_tma_out();
     p.tiles_m = static_cast<int>((M + 255) / 256);
     p.tiles_n = static_cast<int>((N + bn2 - 1) / bn2);
     p.split = 1;
@@ -1012,15 +1092,15 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     const int pairs = static_cast<int>(tiles < sms / 2 ? tiles : sms / 2);
     const int grid = 2 * pairs;
     if (bn2 == 128) {
-      if (b_kmajor) return bf16 ? (resid ? launch_tc2<128, false, true, true>(ta, tb, p, grid, stream) : launch_tc2<128, false, false, true>(ta, tb, p, grid, stream))
-                                : (resid ? launch_tc2<128, false, true, false>(ta, tb, p, grid, stream) : launch_tc2<128, false, false, false>(ta, tb, p, grid, stream));
-      return bf16 ? (resid ? launch_tc2<128, true, true, true>(ta, tb, p, grid, stream) : launch_tc2<128, true, false, true>(ta, tb, p, grid, stream))
-                  : (resid ? launch_tc2<128, true, true, false>(ta, tb, p, grid, stream) : launch_tc2<128, true, false, false>(ta, tb, p, grid, stream));
+      if (b_kmajor) return bf16 ? (resid ? launch_tc2<128, false, true, true>(ta, tb, tc, p, grid, stream) : launch_tc2<128, false, false, true>(ta, tb, tc, p, grid, stream))
+                                : (resid ? launch_tc2<128, false, true, false>(ta, tb, tc, p, grid, stream) : launch_tc2<128, false, false, false>(ta, tb, tc, p, grid, stream));
+      return bf16 ? (resid ? launch_tc2<128, true, true, true>(ta, tb, tc, p, grid, stream) : launch_tc2<128, true, false, true>(ta, tb, tc, p, grid, stream))
+                  : (resid ? launch_tc2<128, true, true, false>(ta, tb, tc, p, grid, stream) : launch_tc2<128, true, false, false>(ta, tb, tc, p, grid, stream));
     }
-    if (b_kmajor) return bf16 ? (resid ? launch_tc2<256, false, true, true>(ta, tb, p, grid, stream) : launch_tc2<256, false, false, true>(ta, tb, p, grid, stream))
-                              : (resid ? launch_tc2<256, false, true, false>(ta, tb, p, grid, stream) : launch_tc2<256, false, false, false>(ta, tb, p, grid, stream));
-    return bf16 ? (resid ? launch_tc2<256, true, true, true>(ta, tb, p, grid, stream) : launch_tc2<256, true, false, true>(ta, tb, p, grid, stream))
-                : (resid ? launch_tc2<256, true, true, false>(ta, tb, p, grid, stream) : launch_tc2<256, true, false, false>(ta, tb, p, grid, stream));
+    if (b_kmajor) return bf16 ? (resid ? launch_tc2<256, false, true, true>(ta, tb, tc, p, grid, stream) : launch_tc2<256, false, false, true>(ta, tb, tc, p, grid, stream))
+                              : (resid ? launch_tc2<256, false, true, false>(ta, tb, tc, p, grid, stream) : launch_tc2<256, false, false, false>(ta, tb, tc, p, grid, stream));
+    return bf16 ? (resid ? launch_tc2<256, true, true, true>(ta, tb, tc, p, grid, stream) : launch_tc2<256, true, false, true>(ta, tb, tc, p, grid, stream))
+                : (resid ? launch_tc2<256, true, true, false>(ta, tb, tc, p, grid, stream) : launch_tc2<256, true, false, false>(ta, tb, tc, p, grid, stream));
   }
 
   // General persistent GEMM: 128 x BN output tiles.
@@ -1041,6 +1121,7 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
                       static_cast<uint64_t>(N), kBK, 64))
       return ENGINE_ERR_UNSUPPORTED;
   }
+  enable_tma_out();
   p.tiles_m = static_cast<int>((M + kBM - 1) / kBM);
   p.tiles_n = static_cast<int>((N + bn - 1) / bn);
   p.split = 1;
@@ -1050,15 +1131,15 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   if (b_kmajor) {
     switch (bn) {
-      case 64: return bf16 ? launch_tc_r<64, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, false, false, false, false>(resid, ta, tb, p, grid, stream);
-      case 128: return bf16 ? launch_tc_r<128, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<128, false, false, false, false>(resid, ta, tb, p, grid, stream);
-      default: return bf16 ? launch_tc_r<256, false, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<256, false, false, false, false>(resid, ta, tb, p, grid, stream);
+      case 64: return bf16 ? launch_tc_r<64, false, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<64, false, false, false, false>(resid, ta, tb, tc, p, grid, stream);
+      case 128: return bf16 ? launch_tc_r<128, false, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<128, false, false, false, false>(resid, ta, tb, tc, p, grid, stream);
+      default: return bf16 ? launch_tc_r<256, false, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<256, false, false, false, false>(resid, ta, tb, tc, p, grid, stream);
     }
   }
   switch (bn) {
-    case 64: return bf16 ? launch_tc_r<64, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<64, true, false, false, false>(resid, ta, tb, p, grid, stream);
-    case 128: return bf16 ? launch_tc_r<128, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<128, true, false, false, false>(resid, ta, tb, p, grid, stream);
-    default: return bf16 ? launch_tc_r<256, true, false, false, true>(resid, ta, tb, p, grid, stream) : launch_tc_r<256, true, false, false, false>(resid, ta, tb, p, grid, stream);
+    case 64: return bf16 ? launch_tc_r<64, true, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<64, true, false, false, false>(resid, ta, tb, tc, p, grid, stream);
+    case 128: return bf16 ? launch_tc_r<128, true, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<128, true, false, false, false>(resid, ta, tb, tc, p, grid, stream);
+    default: return bf16 ? launch_tc_r<256, true, false, false, true>(resid, ta, tb, tc, p, grid, stream) : launch_tc_r<256, true, false, false, false>(resid, ta, tb, tc, p, grid, stream);
   }
 }
 
