@@ -40,6 +40,9 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -70,6 +73,12 @@ struct TcParams {
   int tma_epi;           // output written by TMA stores through shared memory
   unsigned int* err;
   unsigned long long limit_ns;
+  // Stream-K schedule of the 2-SM kernel (sk_iters == 0: whole tiles only).
+  int64_t dp_tiles;             // tiles handed out whole, round-robin over CTA pairs
+  int64_t sk_iters;             // k-blocks of the remaining tiles, split evenly over pairs
+  float* ws;                    // FP32 partial-tile slots: [pair][2][rank][128 x BN]
+  unsigned long long* ws_cnt;   // arrival counters: [stream-K tile][rank]
+  unsigned int ws_gen;          // launch tag carried in the counters' high word
 #ifdef ENGINE_TC_TRACE
   unsigned long long* trace;  // debug builds: 8 timestamps per CTA
 #endif
@@ -161,6 +170,131 @@ __device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n,
   tn = static_cast<int>(r / gsize);
 }
 
+// ---------------------------------------------------------------- stream-K
+// The 2-SM kernel's work list for CTA pair q: first the whole tiles
+// q, q + P, ... below dp_tiles (P = pairs in the grid), then the k-block range
+// [b(q), b(q+1)), b(q) = q * sk_iters / P, of the stream-K region -- the last
+// sk_iters / num_kb tiles laid end to end along K.  The host keeps that region
+// between P and 2P tiles, so every range spans num_kb..2*num_kb k-blocks, has at
+// most three segments, and no tile is shared by more than two pairs.  A segment
+// that covers a whole tile is stored like a round-robin tile.  A partial
+// segment parks its FP32 accumulator in a workspace slot and arrives on the
+// tile's counter; the second arriver adds the two partials in pair order (so
+// the sum does not depend on which pair finishes first) and stores the tile.
+// Nothing waits on another CTA.
+struct TcWork {
+  int64_t tile;     // linear tile index (tile_coords order)
+  int64_t kb0, kb1; // k-block range of this segment
+  int64_t sk_tile;  // -1: whole tile; else tile index within the stream-K region
+};
+
+__device__ __forceinline__ int64_t sk_bound(const TcParams& p, int64_t q, int64_t npairs) {
+  return q * p.sk_iters / npairs;
+}
+
+/// The pair whose range holds stream-K k-block `i` (largest q with b(q) <= i).
+__device__ __forceinline__ int64_t sk_owner(const TcParams& p, int64_t i, int64_t npairs) {
+  int64_t q = i * npairs / p.sk_iters;  // b(q) <= i already; step up past equal bounds
+  while (q + 1 < npairs && sk_bound(p, q + 1, npairs) <= i) ++q;
+  return q;
+}
+
+struct TcSched {
+  int64_t t, it, it_end;
+  __device__ TcSched(const TcParams& p, int64_t pair, int64_t npairs) : t(pair) {
+    it = p.sk_iters > 0 ? sk_bound(p, pair, npairs) : 0;
+    it_end = p.sk_iters > 0 ? sk_bound(p, pair + 1, npairs) : 0;
+  }
+  __device__ bool next(const TcParams& p, int64_t npairs, TcWork& w) {
+    if (t < p.dp_tiles) {
+      w.tile = t;
+      w.kb0 = 0;
+      w.kb1 = p.num_kb;
+      w.sk_tile = -1;
+      t += npairs;
+      return true;
+    }
+    if (it >= it_end) return false;
+    const int64_t tl = it / p.num_kb;
+    const int64_t end = it_end - tl * p.num_kb;
+    w.tile = p.dp_tiles + tl;
+    w.kb0 = it - tl * p.num_kb;
+    w.kb1 = end < p.num_kb ? end : p.num_kb;
+    w.sk_tile = (w.kb0 == 0 && w.kb1 == p.num_kb) ? -1 : tl;
+    it = tl * p.num_kb + w.kb1;
+    return true;
+  }
+};
+
+/// One CTA's partial slot: 128 rows x BN FP32 columns, stored as float4 units
+/// [BN/4 column quads][128 rows] so that the 32 lanes of a warp (32 consecutive
+/// rows) move 512 contiguous bytes per access.
+template <int BN>
+__device__ __forceinline__ float* sk_slot(const TcParams& p, int64_t pair, int slot,
+                                          uint32_t rank) {
+  return p.ws + ((pair * 2 + slot) * 2 + rank) * static_cast<int64_t>(128 * BN);
+}
+
+/// Partial slot (0: first segment of the pair's range, 1: last) that pair q used
+/// for stream-K tile tl.
+__device__ __forceinline__ int sk_slot_of(const TcParams& p, int64_t q, int64_t tl,
+                                          int64_t npairs) {
+  return (sk_bound(p, q, npairs) / p.num_kb == tl) ? 0 : 1;
+}
+
+/// Counts this CTA's arrival on a stream-K tile counter and returns the arrival
+/// number (1-based).  The high word carries the launch tag: a count left by an
+/// aborted launch (device time-out) is not mistaken for this launch's.  Release
+/// of this CTA's parked partial and acquire of the other's are both on the CAS.
+__device__ __forceinline__ uint32_t sk_arrive(unsigned long long* cnt, uint32_t gen,
+                                              unsigned int* err) {
+  unsigned long long old;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(old) : "l"(cnt) : "memory");
+  for (int tries = 0; tries < 4096; ++tries) {
+    const uint32_t c = (static_cast<uint32_t>(old >> 32) == gen) ? static_cast<uint32_t>(old) + 1 : 1u;
+    const unsigned long long nv = (static_cast<unsigned long long>(gen) << 32) | c;
+    unsigned long long prev;
+    asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;"
+                 : "=l"(prev)
+                 : "l"(cnt), "l"(old), "l"(nv)
+                 : "memory");
+    if (prev == old) return c;
+    old = prev;
+  }
+  atomicOr(err, kErrWaitTimeout);  // a CAS that never wins: report, do not loop on
+  return 0;
+}
+
+__device__ __forceinline__ void sk_reset(unsigned long long* cnt) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(cnt), "l"(0ull) : "memory");
+}
+
+/// Address of columns 4q..4q+3 of row rl in a partial slot.
+__device__ __forceinline__ float4* sk_quad(float* slot, int quad, int rl) {
+  return reinterpret_cast<float4*>(slot) + quad * 128 + rl;
+}
+
+/// Loads columns c..c+31 of row rl of the other pair's parked partial.
+__device__ __forceinline__ void sk_load32(float4 x[8], const float* other, int c, int rl) {
+  const float4* o = reinterpret_cast<const float4*>(other) + (c >> 2) * 128 + rl;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x[j] = __ldcg(o + j * 128);
+}
+
+/// Adds the other pair's partial (x, from sk_load32) to 32 accumulator values
+/// of this CTA (still in TMEM).  With two contributors the sum is one IEEE
+/// addition, which is commutative: the result does not depend on which pair
+/// arrived last.
+__device__ __forceinline__ void sk_add32(uint32_t v[32], const float4 x[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j * 4 + 0] = __float_as_uint(__uint_as_float(v[j * 4 + 0]) + x[j].x);
+    v[j * 4 + 1] = __float_as_uint(__uint_as_float(v[j * 4 + 1]) + x[j].y);
+    v[j * 4 + 2] = __float_as_uint(__uint_as_float(v[j * 4 + 2]) + x[j].z);
+    v[j * 4 + 3] = __float_as_uint(__uint_as_float(v[j * 4 + 3]) + x[j].w);
+  }
+}
+
 /// Writes one output element of the tile: (rl, j) = (tile row, tile column).
 template <bool SWAP, bool RESID, bool BF16>
 __device__ __forceinline__ void emit(const TcParams& p, int tm, int tn, int rl, int j, int bn,
@@ -184,12 +318,73 @@ __device__ __forceinline__ void emit(const TcParams& p, int tm, int tn, int rl, 
 /// swizzled 16 KB staging tile (conflict-free 16-byte writes), then one thread
 /// stores the tile with a TMA bulk-tensor store.  Two staging tiles alternate;
 /// `chunk` counts staged chunks across tiles.  TMA clips rows / columns
-/// outside the output, so edge tiles need no special case.
+/// outside the output, so edge tiles need no special case.  `other` (non-null:
+/// stream-K fix-up) is the other pair's parked partial of this tile.
+/// Converts 64 accumulator columns (v) into the swizzled staging tile `buf` and
+/// has the elected thread store it.
+template <bool BF16>
+__device__ __forceinline__ void epilogue_stage_store(const CUtensorMap* tmC, uint8_t* buf,
+                                                     const uint32_t (&v)[2][32], int rl,
+                                                     bool elect, int32_t col, int32_t row0) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t* w = &v[j >> 2][(j & 3) * 8];
+    uint4 o;
+    o.x = pack2<BF16>(__uint_as_float(w[0]), __uint_as_float(w[1]));
+    o.y = pack2<BF16>(__uint_as_float(w[2]), __uint_as_float(w[3]));
+    o.z = pack2<BF16>(__uint_as_float(w[4]), __uint_as_float(w[5]));
+    o.w = pack2<BF16>(__uint_as_float(w[6]), __uint_as_float(w[7]));
+    *reinterpret_cast<uint4*>(buf + rl * 128 + ((j ^ (rl & 7)) << 4)) = o;
+  }
+  fence_proxy_async_smem();
+  named_barrier_sync(1, 128);
+  if (elect) {
+    tma_store_2d(tmC, buf, col, row0);
+    bulk_commit_group();
+  }
+}
+
+/// Stream-K fix-up form of epilogue_tma_tile: adds the other pair's parked
+/// partial of the tile.  The partial's loads run one 64-column chunk ahead of
+/// the conversion, so two chunks (32 KB per warp group) are in flight.
+template <int BN, bool BF16>
+__device__ __forceinline__ void epilogue_tma_tile_fix(const CUtensorMap* tmC, uint8_t* stage,
+                                                      uint32_t taddr, int rl, bool elect,
+                                                      int32_t col_base, int32_t row0,
+                                                      uint32_t& chunk, const float* other) {
+  float4 x[2][2][8];
+  sk_load32(x[0][0], other, 0, rl);
+  sk_load32(x[0][1], other, 32, rl);
+#pragma unroll
+  for (int c = 0; c < BN; c += 64, ++chunk) {
+    const int cur = (c >> 6) & 1;
+    if (c + 64 < BN) {
+      sk_load32(x[cur ^ 1][0], other, c + 64, rl);
+      sk_load32(x[cur ^ 1][1], other, c + 96, rl);
+    }
+    uint8_t* buf = stage + (chunk & 1u) * kEpiStageBytes;
+    if (elect) bulk_wait_group_read<1>();
+    named_barrier_sync(1, 128);
+    uint32_t v[2][32];
+    tmem_ld_32x32b_x32(taddr + c, v[0]);
+    tmem_ld_32x32b_x32(taddr + c + 32, v[1]);
+    tmem_wait_ld();
+    sk_add32(v[0], x[cur][0]);
+    sk_add32(v[1], x[cur][1]);
+    epilogue_stage_store<BF16>(tmC, buf, v, rl, elect, col_base + c, row0);
+  }
+}
+
 template <int BN, bool BF16>
 __device__ __forceinline__ void epilogue_tma_tile(const CUtensorMap* tmC, uint8_t* stage,
                                                   uint32_t taddr, int rl, bool elect,
                                                   int32_t col_base, int32_t row0,
-                                                  uint32_t& chunk) {
+                                                  uint32_t& chunk,
+                                                  const float* other = nullptr) {
+  if (other != nullptr) {
+    epilogue_tma_tile_fix<BN, BF16>(tmC, stage, taddr, rl, elect, col_base, row0, chunk, other);
+    return;
+  }
 #pragma unroll 1
   for (int c = 0; c < BN; c += 64, ++chunk) {
     uint8_t* buf = stage + (chunk & 1u) * kEpiStageBytes;
@@ -199,22 +394,7 @@ __device__ __forceinline__ void epilogue_tma_tile(const CUtensorMap* tmC, uint8_
     tmem_ld_32x32b_x32(taddr + c, v[0]);
     tmem_ld_32x32b_x32(taddr + c + 32, v[1]);
     tmem_wait_ld();
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t* w = &v[j >> 2][(j & 3) * 8];
-      uint4 o;
-      o.x = pack2<BF16>(__uint_as_float(w[0]), __uint_as_float(w[1]));
-      o.y = pack2<BF16>(__uint_as_float(w[2]), __uint_as_float(w[3]));
-      o.z = pack2<BF16>(__uint_as_float(w[4]), __uint_as_float(w[5]));
-      o.w = pack2<BF16>(__uint_as_float(w[6]), __uint_as_float(w[7]));
-      *reinterpret_cast<uint4*>(buf + rl * 128 + ((j ^ (rl & 7)) << 4)) = o;
-    }
-    fence_proxy_async_smem();
-    named_barrier_sync(1, 128);
-    if (elect) {
-      tma_store_2d(tmC, buf, col_base + c, row0);
-      bulk_commit_group();
-    }
+    epilogue_stage_store<BF16>(tmC, buf, v, rl, elect, col_base + c, row0);
   }
 }
 
@@ -579,11 +759,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + ST;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* sk_flag = tmem_slot + 1;  // stream-K: this CTA stores the tile
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 = leader
   const bool leader = rank == 0;
+  if (threadIdx.x == 0) TC_TRACE(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -610,8 +792,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_trigger();
   pdl_wait();
+  if (threadIdx.x == 0) TC_TRACE(1);
 
-  const int64_t num_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   const int64_t pair = blockIdx.x >> 1;
   const int64_t npairs = gridDim.x >> 1;
   const int64_t nkb = p.num_kb;
@@ -622,10 +804,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
       uint32_t it = 0;
       bool ok = true;
-      for (int64_t t = pair; ok && t < num_tiles; t += npairs) {
+      TcSched sch(p, pair, npairs);
+      TcWork w;
+      while (ok && sch.next(p, npairs, w)) {
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
+        for (int64_t kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const uint32_t s = it % ST;
           const uint32_t ph = (it / ST) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, p.limit_ns, p.err)) {
@@ -661,13 +845,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tfull_self0 = mapa_shared(smem_u32(&tfull[0]), 0);
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (int64_t t = pair; ok && t < num_tiles; t += npairs, ++tl) {
+      TcSched sch(p, pair, npairs);
+      TcWork w;
+      for (; ok && sch.next(p, npairs, w); ++tl) {
         const uint32_t a = tl & 1u;
         const uint32_t aph = (tl >> 1) & 1u;
         if (!mbar_wait(&tempty[a], aph ^ 1u, p.limit_ns, p.err)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
-        for (int64_t kb = 0; kb < nkb; ++kb, ++it) {
+#ifdef ENGINE_TC_TRACE
+        if (w.tile >= p.dp_tiles && p.trace && p.trace[blockIdx.x * 8 + 2] == 0) TC_TRACE(2);
+#endif
+        for (int64_t kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const uint32_t s = it % ST;
           const uint32_t ph = (it / ST) & 1u;
           if (!mbar_wait(&full[s], ph, p.limit_ns, p.err)) {
@@ -686,7 +875,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               bdesc = umma_desc_sw128(sb + kk * 32, 16, 1024);
             }
-            umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_2sm(d_tmem, adesc, bdesc, kIdesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit_2sm(empty_self0 + s * 8);
           umma_commit_2sm(empty_peer0 + s * 8);
@@ -695,6 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit_2sm(tfull_self0 + a * 8);
         umma_commit_2sm(tfull_peer0 + a * 8);
       }
+      TC_TRACE(3);
     }
     __syncwarp();
   } else {
@@ -703,20 +893,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     uint32_t tl = 0;
     uint32_t epi_chunk = 0;
-    for (int64_t t = pair; t < num_tiles; t += npairs, ++tl) {
+    TcSched sch(p, pair, npairs);
+    TcWork w;
+    for (; sch.next(p, npairs, w); ++tl) {
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
       const uint32_t a = tl & 1u;
       const uint32_t aph = (tl >> 1) & 1u;
       if (!mbar_wait(&tfull[a], aph, p.limit_ns, p.err)) break;
       tc_fence_after();
+      if (warp == 2 && lane == 0) TC_TRACE(5);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * BN;
       const int64_t row = static_cast<int64_t>(tm) * 256 + static_cast<int64_t>(rank) * 128 + rl;
+      const float* other = nullptr;  // stream-K: the other pair's partial of this tile
+      if (w.sk_tile >= 0) {
+        // The second of the tile's two pairs to arrive stores the tile.  If the
+        // other pair has already parked its partial, this CTA stores the tile
+        // at once; otherwise it parks its own partial and arrives, and whichever
+        // arrival comes second does the store.
+        unsigned long long* cnt = p.ws_cnt + w.sk_tile * 2 + rank;
+        if (warp == 2 && lane == 0) {
+          unsigned long long v;
+          asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(cnt) : "memory");
+          const bool second = static_cast<uint32_t>(v >> 32) == p.ws_gen && static_cast<uint32_t>(v) == 1u;
+          if (second) sk_reset(cnt);
+          *sk_flag = second ? 1u : 0u;
+        }
+        named_barrier_sync(1, 128);
+        if (*reinterpret_cast<volatile uint32_t*>(sk_flag) == 0u) {
+          float* mine = sk_slot<BN>(p, pair, sk_slot_of(p, pair, w.sk_tile, npairs), rank);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __stcg(sk_quad(mine, (c >> 2) + j, rl),
+                     make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])));
+            }
+          }
+          named_barrier_sync(1, 128);
+          if (warp == 2 && lane == 0) {
+            const uint32_t n = sk_arrive(cnt, p.ws_gen, p.err);
+            if (n == 2) sk_reset(cnt);
+            *sk_flag = (n == 2) ? 1u : 0u;
+          }
+          named_barrier_sync(1, 128);
+          if (*reinterpret_cast<volatile uint32_t*>(sk_flag) == 0u) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
+            continue;
+          }
+        }
+        if (warp == 2 && lane == 0) TC_TRACE(6);
+        const int64_t first = sk_owner(p, w.sk_tile * nkb, npairs);
+        const int64_t q_other = (first == pair) ? pair + 1 : first;
+        other = sk_slot<BN>(p, q_other, sk_slot_of(p, q_other, w.sk_tile, npairs), rank);
+      }
       if constexpr (!RESID) {
         if (p.tma_epi) {
           epilogue_tma_tile<BN, BF16>(&tmC, epi_stage, taddr, rl, warp == 2 && lane == 0,
                                       tn * BN, tm * 256 + static_cast<int>(rank) * 128,
-                                      epi_chunk);
+                                      epi_chunk, other);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
@@ -726,8 +967,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
+        float4 x[8];
+        if (other != nullptr) sk_load32(x, other, c, rl);
         tmem_ld_32x32b_x32(taddr + c, v);
         tmem_wait_ld();
+        if (other != nullptr) sk_add32(v, x);
         const int64_t col0 = static_cast<int64_t>(tn) * BN + c;
         if (row < p.out_rows) {
           float f[32];
@@ -781,7 +1025,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + a * 8);
     }
-    if (warp == 2 && lane == 0) bulk_wait_group<0>();  // TMA stores complete before exit
+    if (warp == 2 && lane == 0) {
+      bulk_wait_group<0>();  // TMA stores complete before exit
+      TC_TRACE(4);
+    }
   }
 
   tc_fence_before();
@@ -791,6 +1038,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_2sm(tmem_base, Cfg::kTmemCols);
   }
+#ifdef ENGINE_TC_TRACE
+  if (threadIdx.x == 0 && p.trace) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    TC_TRACE(7);
+    p.trace[blockIdx.x * 8 + 7] = (p.trace[blockIdx.x * 8 + 7] << 8) | smid;
+  }
+#endif
 }
 
 // ------------------------------------------------------------------ host side
@@ -896,6 +1151,52 @@ int env_int(const char* name, int dflt) {
   const char* e = std::getenv(name);
   if (e == nullptr || e[0] == '\0') return dflt;
   return static_cast<int>(std::strtol(e, nullptr, 10));
+}
+
+// Stream-K workspace of the 2-SM kernel, one per (device, stream): calls on one
+// stream run one after another, so their partial slots and counters never
+// overlap; calls on different streams get different workspaces.  Sized for the
+// largest grid (one pair slot pair per 2 SMs, BN = 256) and kept for the life of
+// the process.  Counters start at zero and every completed launch leaves them
+// at zero, so a CUDA graph may replay a captured launch.  The first call on a
+// stream allocates; a call made during stream capture before that falls back
+// to whole-tile scheduling.
+struct SkWorkspace {
+  float* parts = nullptr;
+  unsigned long long* cnt = nullptr;
+  unsigned int gen = 0;
+};
+
+bool sk_workspace(int dev, cudaStream_t stream, int max_pairs, float** parts,
+                  unsigned long long** cnt, unsigned int* gen) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, SkWorkspace> spaces;
+  std::lock_guard<std::mutex> lk(mu);
+  SkWorkspace& w = spaces[std::make_pair(dev, stream)];
+  if (w.parts == nullptr) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      return false;
+    const size_t part_bytes = static_cast<size_t>(max_pairs) * 2 * 2 * 128 * 256 * sizeof(float);
+    const size_t cnt_bytes = static_cast<size_t>(2 * max_pairs) * 2 * sizeof(unsigned long long);
+    void* mem = nullptr;
+    if (cudaMalloc(&mem, part_bytes + cnt_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (cudaMemset(reinterpret_cast<uint8_t*>(mem) + part_bytes, 0, cnt_bytes) != cudaSuccess) {
+      cudaFree(mem);
+      cudaGetLastError();
+      return false;
+    }
+    w.parts = reinterpret_cast<float*>(mem);
+    w.cnt = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(mem) + part_bytes);
+  }
+  if (++w.gen == 0) w.gen = 1;  // 0 never tags a live count
+  *parts = w.parts;
+  *cnt = w.cnt;
+  *gen = w.gen;
+  return true;
 }
 
 // 16-bit GEMM on CUDA cores for shapes TMA cannot describe (row pitch not a
@@ -1091,6 +1392,23 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
     const int pairs = static_cast<int>(tiles < sms / 2 ? tiles : sms / 2);
     const int grid = 2 * pairs;
+    // Whole tiles round-robin, unless the last wave would leave >= 1/16 of the
+    // pairs idle: then all but one full wave stays round-robin and the rest
+    // (between `pairs` and 2 * `pairs` tiles) is split along K evenly.
+    p.dp_tiles = tiles;
+    p.sk_iters = 0;
+    static const int streamk_env = env_int("ENGINE_TC_STREAMK", 1);
+    const int64_t waves = tiles / pairs;
+    const int64_t rem = tiles % pairs;
+    if (streamk_env != 0 && waves >= 1 && rem != 0 && (pairs - rem) * 16 >= pairs &&
+        p.num_kb >= 8) {
+      int dev = 0;
+      B200_CUDA(cudaGetDevice(&dev));
+      if (sk_workspace(dev, stream, sms / 2, &p.ws, &p.ws_cnt, &p.ws_gen)) {
+        p.dp_tiles = (waves - 1) * pairs;
+        p.sk_iters = (tiles - p.dp_tiles) * p.num_kb;
+      }
+    }
     if (bn2 == 128) {
       if (b_kmajor) return bf16 ? (resid ? launch_tc2<128, false, true, true>(ta, tb, tc, p, grid, stream) : launch_tc2<128, false, false, true>(ta, tb, tc, p, grid, stream))
                                 : (resid ? launch_tc2<128, false, true, false>(ta, tb, tc, p, grid, stream) : launch_tc2<128, false, false, false>(ta, tb, tc, p, grid, stream));

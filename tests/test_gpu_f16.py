@@ -122,6 +122,64 @@ def test_matmul_f16_4096_cubed_sampled_rows(pkg, dev):
     check_linear(C, host(A), np.ascontiguousarray(host(B).T), None, rows, what="4096^3")
 
 
+# Shapes whose 256 x 256 tile count leaves a partial last wave on 74 CTA pairs, so
+# the 2-SM kernel splits the last tiles along K (stream-K) and the second pair
+# to finish a shared tile adds the other's parked partial.  N % 8 != 0 turns
+# the TMA-store epilogue off, so both epilogue paths do the fix-up.
+@pytest.mark.parametrize("M,N,K,resid", [(2304, 2304, 512, False), (2300, 2310, 520, False),
+                                         (2304, 2304, 1000, True)])
+def test_linear_f16_stream_k_tiles(pkg, dev, M, N, K, resid):
+    rng = np.random.default_rng(M + N + K)
+    X = f16(rng, (M, K))
+    W = f16(rng, (N, K), 0.05)
+    R = f16(rng, (M, N)) if resid else None
+    Y = torch.empty(M, N, device=dev, dtype=torch.float16)
+    pkg.cuda.linear_f16(dev_t(X).data_ptr(), dev_t(W).data_ptr(),
+                        dev_t(R).data_ptr() if resid else 0, Y.data_ptr(), M, N, K)
+    check_linear(Y, X, W, R, np.arange(M), what=f"stream-K {M}x{N}x{K}")
+
+
+def test_matmul_bf16_stream_k_tiles(pkg, dev):
+    M, N, K = 2304, 2560, 640
+    rng = np.random.default_rng(5)
+    A = bf16_bits(rng, (M, K))
+    B = bf16_bits(rng, (K, N))
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    pkg.cuda.matmul_bf16(dev_t(A).data_ptr(), dev_t(B).data_ptr(), C.data_ptr(), M, N, K)
+    check_linear(C.view(torch.int16), A, np.ascontiguousarray(B.T), None, np.arange(M),
+                 bf16=True, what="bf16 stream-K")
+
+
+def test_matmul_f16_stream_k_deterministic_and_graph_replay(pkg, dev):
+    """4096^3 runs stream-K on a full B200; repeated eager calls and CUDA graph
+    replays of a captured call (the tile counters reset themselves) agree bit
+    for bit."""
+    M = N = K = 4096
+    g = torch.Generator(device="cuda").manual_seed(3)
+    A = torch.randn(M, K, device=dev, generator=g).half()
+    B = torch.randn(K, N, device=dev, generator=g).half()
+    C1 = torch.empty(M, N, device=dev, dtype=torch.float16)
+    C2 = torch.empty_like(C1)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        pkg.cuda.matmul_f16(A.data_ptr(), B.data_ptr(), C1.data_ptr(), M, N, K, s.cuda_stream)
+        pkg.cuda.matmul_f16(A.data_ptr(), B.data_ptr(), C2.data_ptr(), M, N, K, s.cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(C1, C2)
+    C3 = torch.zeros_like(C1)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        pkg.cuda.matmul_f16(A.data_ptr(), B.data_ptr(), C3.data_ptr(), M, N, K, s.cuda_stream)
+    for _ in range(3):
+        C3.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(C1, C3)
+    del graph
+    rows = sample_rows(M, 24, seed=3)
+    check_linear(C1, host(A), np.ascontiguousarray(host(B).T), None, rows, what="4096^3 sk")
+
+
 def test_matmul_f16_deterministic(pkg, dev):
     M = N = K = 1024
     g = torch.Generator(device="cuda").manual_seed(1)
