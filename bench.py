@@ -464,7 +464,8 @@ def run_headline(args):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": achieved / peak_t, "traffic": traffic,
                      "peak_kind": f"{pk_kind} bf16 dense burst",
-                     "kernel": "gemm_tc_kernel 4096^3", "kernel_ms": gemm_kernel_ms},
+                     "kernel": "gemm_tc2_kernel<256> 4096^3 (2-SM tcgen05, 256x256 tiles, stream-K tail)",
+                     "kernel_ms": gemm_kernel_ms},
         "gemv": {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / pk["hbm_gbs"],
                  "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
                  "kernel_us": gemv_kernel_ms * 1e3, "job_gbs": gemv_job,
