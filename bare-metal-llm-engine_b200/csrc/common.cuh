@@ -111,6 +111,11 @@ namespace b200 {
 constexpr unsigned int kErrWaitTimeout = 1u;   // an mbarrier / cluster wait ran out
 constexpr unsigned int kErrBadArgument = 2u;   // a kernel's own bounds check fired
 
+// Tensor-parallel communicator (tp_comm.cu): largest world and the fixed grid of
+// every communicator kernel (all CTAs co-resident; per-CTA call counts).
+constexpr int kTpMaxWorld = 8;
+constexpr int kTpCtas = 256;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -24,6 +24,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "kernels.cuh"
 
 namespace cg = cooperative_groups;
@@ -31,35 +32,13 @@ namespace cg = cooperative_groups;
 namespace b200 {
 namespace {
 
-__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ void h8_to_f8(const uint4& v, float (&f)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
-
 // ---------------------------------------------------------------- [N,K] GEMV
 
 constexpr int kNkWarps = 4;     // scalar fallback: one row per warp
-constexpr int kNkVecWarps = 8;  // vector kernel: 8 warps per CTA
 
-// SK warps share one group of RPW weight rows: lane l of warp `sub` streams the
-// 16-byte chunks c = sub*32 + l + i*32*SK of every row, so the SK warps of a
-// group read 512*SK contiguous bytes per step.  Loads are software-pipelined
-// (two register buffers of U chunks per row: the next U chunks are in flight
-// while the current ones are multiplied).  Partial sums are reduced with warp
-// shuffles, then across the SK warps in fixed order through shared memory.
+// Decode GEMV kernel: one row block per CTA (nk_block_dots), then the SK
+// partial sums of each row are added in fixed order, scaled by the RMS factor
+// when NORM, plus the residual, rounded once to FP16.
 template <int MR, int RPW, int SK, int U, bool NORM, bool RESID>
 __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
     const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
@@ -67,112 +46,10 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
   constexpr int GROUPS = kNkVecWarps / SK;
   constexpr int NACC = MR * RPW + (NORM ? MR : 0);
   __shared__ float red[kNkVecWarps][NACC];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int grp = warp / SK;
-  const int sub = warp % SK;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * GROUPS + grp) * RPW;
-  const int64_t nchunk = K >> 3;  // 8 halves per 16-byte chunk
-  constexpr int64_t kStride = 32 * SK;
-
-  float acc[MR][RPW];
-  float ss[MR];
-#pragma unroll
-  for (int m = 0; m < MR; ++m) {
-    ss[m] = 0.0f;
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[m][r] = 0.0f;
-  }
   pdl_trigger();
+  nk_block_prefetch<RPW, SK, U>(W, N, K, blockIdx.x);
   pdl_wait();
-
-  if (row0 < N) {
-    const __half* wrow[RPW];
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: never stored
-      wrow[r] = W + n * K;
-    }
-    uint4 wa[U][RPW], xa[U][MR], ga[U];
-    uint4 wb[U][RPW], xb[U][MR], gb[U];
-    auto load = [&](int64_t c0, uint4 (&w)[U][RPW], uint4 (&x)[U][MR], uint4 (&g)[U]) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t c = c0 + kStride * u;
-        if (c < nchunk) {
-#pragma unroll
-          for (int r = 0; r < RPW; ++r) w[u][r] = ld_stream_v4(wrow[r] + 8 * c);
-#pragma unroll
-          for (int m = 0; m < MR; ++m)
-            x[u][m] = __ldg(reinterpret_cast<const uint4*>(X + m * K + 8 * c));
-          if constexpr (NORM) {
-            g[u] = gamma ? __ldg(reinterpret_cast<const uint4*>(gamma + 8 * c))
-                         : make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
-          }
-        }
-      }
-    };
-    auto compute = [&](int64_t c0, uint4 (&w)[U][RPW], uint4 (&x)[U][MR], uint4 (&g)[U]) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t c = c0 + kStride * u;
-        if (c < nchunk) {
-          float gf[8];
-          if constexpr (NORM) h8_to_f8(g[u], gf);
-#pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            float xf[8];
-            h8_to_f8(x[u][m], xf);
-            if constexpr (NORM) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                ss[m] = fmaf(xf[i], xf[i], ss[m]);
-                xf[i] *= gf[i];
-              }
-            }
-#pragma unroll
-            for (int r = 0; r < RPW; ++r) {
-              float wf[8];
-              h8_to_f8(w[u][r], wf);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) acc[m][r] = fmaf(xf[i], wf[i], acc[m][r]);
-            }
-          }
-        }
-      }
-    };
-    int64_t c0 = sub * 32 + lane;
-    load(c0, wa, xa, ga);
-    for (; c0 < nchunk; c0 += 2 * kStride * U) {
-      const int64_t c1 = c0 + kStride * U;
-      load(c1, wb, xb, gb);
-      compute(c0, wa, xa, ga);
-      load(c1 + kStride * U, wa, xa, ga);
-      compute(c1, wb, xb, gb);
-    }
-  }
-
-#pragma unroll
-  for (int m = 0; m < MR; ++m) {
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[m][r] += __shfl_xor_sync(0xffffffffu, acc[m][r], o);
-    }
-    if constexpr (NORM) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss[m] += __shfl_xor_sync(0xffffffffu, ss[m], o);
-    }
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int m = 0; m < MR; ++m) {
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) red[warp][m * RPW + r] = acc[m][r];
-      if constexpr (NORM) red[warp][MR * RPW + m] = ss[m];
-    }
-  }
-  __syncthreads();
+  nk_block_dots<MR, RPW, SK, U, NORM>(W, X, gamma, N, K, blockIdx.x, red);
   for (int o = threadIdx.x; o < GROUPS * MR * RPW; o += blockDim.x) {
     const int g = o / (MR * RPW);
     const int rem = o % (MR * RPW);
@@ -236,8 +113,18 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
   };
   int64_t c0 = sub * 32 + lane;
   pdl_trigger();
+  if (active) {  // warm L2 with the first weight chunks while the preceding kernel drains
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t c = c0 + kStride * u;
+      if (c < nchunk) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) prefetch_l2(wrow[r] + 8 * c);
+      }
+    }
+  }
   pdl_wait();
-  if (active) load(c0, wa);  // in flight while the prologue runs
+  if (active) load(c0, wa);
 
   // Prologue: t = x * gamma into shared memory, sum of squares of x.
   float ss = 0.0f;

@@ -92,3 +92,48 @@ def rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps, stream=0)
     M <= 32, K <= 16384).  Concurrent calls on unordered streams race."""
     _check(lib().engine_cuda_rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps,
                                                         _s(stream)))
+
+
+# ------------------------------------------------- tensor-parallel communicator
+# engine_tp_* (include/engine_b200.h): no counterpart in the reference.
+
+TP_HANDLE_BYTES = 64
+
+
+def tp_comm_create(rank, world, max_elems) -> int:
+    """Allocates this rank's exchange region on the current device; returns the
+    communicator handle (an int)."""
+    import ctypes
+
+    out = ctypes.c_void_p(0)
+    _check(lib().engine_tp_comm_create(rank, world, max_elems, ctypes.byref(out)))
+    return int(out.value)
+
+
+def tp_comm_handle(comm) -> bytes:
+    import ctypes
+
+    buf = ctypes.create_string_buffer(TP_HANDLE_BYTES)
+    _check(lib().engine_tp_comm_handle(comm, buf))
+    return buf.raw
+
+
+def tp_comm_open(comm, handles: bytes):
+    """handles: world x TP_HANDLE_BYTES bytes in rank order."""
+    import ctypes
+
+    buf = ctypes.create_string_buffer(handles, len(handles))
+    _check(lib().engine_tp_comm_open(comm, buf))
+
+
+def tp_comm_destroy(comm):
+    _check(lib().engine_tp_comm_destroy(comm))
+
+
+def tp_allreduce_f16(comm, partial, residual, y, n, stream=0):
+    _check(lib().engine_tp_allreduce_f16(comm, partial, residual, y, n, _s(stream)))
+
+
+def tp_linear_allreduce_f16(comm, X, W, residual, Y, M, N, K, stream=0):
+    _check(lib().engine_tp_linear_allreduce_f16(comm, X, W, residual, Y, M, N, K, _s(stream)))
+

@@ -24,6 +24,15 @@ keeps every token row independent (a row-sampled oracle stays exact).
 The ``ops`` object performs the projections.  ``CudaOps`` is the product path
 (the CUDA library); tests inject a CPU double to check the sharding and the
 collective sequence on gloo ranks without a GPU.
+
+The all-reduces run through one of two collectives:
+- ``NvlinkComm`` (engine_tp_*), when given and the message fits its capacity
+  (decode).  The O / down projection and its all-reduce are then ONE kernel:
+  every rank pushes its FP32 partial rows to every peer over NVLink and adds
+  the world partials plus the residual in rank order.
+- torch.distributed ``all_reduce`` otherwise (NCCL on GPUs, gloo in the CPU
+  tests).  Prefill messages (16 MiB) take this path, where a ring beats a
+  one-shot push.
 """
 from __future__ import annotations
 
@@ -119,6 +128,72 @@ class CudaOps:
         return self._o.embedding(table, ids, out=out)
 
 
+# ------------------------------------------------------------------ collective
+
+class NvlinkComm:
+    """The library's tensor-parallel communicator on this rank's current GPU.
+
+    The exchange regions' CUDA IPC handles are all-gathered through
+    torch.distributed (``group``); ``max_elems`` bounds the elements of one
+    call (B x d_model for decode).  Every rank must make the same calls in the
+    same order on one stream.
+    """
+
+    def __init__(self, rank: int, world: int, max_elems: int, group=None):
+        from . import cuda as _c
+        from . import ops as _ops
+
+        self._c = _c
+        self._ops = _ops
+        self.rank, self.world, self.max_elems, self.group = rank, world, int(max_elems), group
+        self.handle = _c.tp_comm_create(rank, world, self.max_elems)
+        mine = _c.tp_comm_handle(self.handle)
+        if world > 1:
+            parts = [None] * world
+            dist.all_gather_object(parts, mine, group=group)
+            handles = b"".join(parts)
+        else:
+            handles = mine
+        _c.tp_comm_open(self.handle, handles)
+
+    def fits(self, rows: int, cols: int) -> bool:
+        return rows * cols <= self.max_elems
+
+    def linear_allreduce(self, x, W, residual=None, out=None):
+        """sum over ranks of x_r @ W_r^T (+ residual), on every rank."""
+        o = self._ops
+        o._req(x, torch.float16, "x")
+        o._req(W, torch.float16, "W")
+        if residual is not None:
+            o._req(residual, torch.float16, "residual")
+        M, K = x.shape
+        N = W.shape[0]
+        Y = out if out is not None else torch.empty(M, N, device=x.device, dtype=torch.float16)
+        self._c.tp_linear_allreduce_f16(self.handle, x.data_ptr(), W.data_ptr(),
+                                        o._ptr(residual), Y.data_ptr(), M, N, K, o._stream())
+        return Y
+
+    def allreduce(self, partial, residual=None, out=None):
+        """sum over ranks of partial (+ residual), on every rank."""
+        o = self._ops
+        o._req(partial, torch.float16, "partial")
+        if residual is not None:
+            o._req(residual, torch.float16, "residual")
+        Y = out if out is not None else torch.empty_like(partial)
+        self._c.tp_allreduce_f16(self.handle, partial.data_ptr(), o._ptr(residual), Y.data_ptr(),
+                                 partial.numel(), o._stream())
+        return Y
+
+    def close(self):
+        """Host barrier over the group, then frees the region (every rank)."""
+        if self.handle:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._c.tp_comm_destroy(self.handle)
+            self.handle = 0
+
+
 # ------------------------------------------------------------------ model
 
 class TPLayerSet:
@@ -130,8 +205,9 @@ class TPLayerSet:
     """
 
     def __init__(self, cfg: TPConfig, rank: int, world: int, layers: list, lm_head, embed,
-                 final_norm, ops=None, group=None):
+                 final_norm, ops=None, group=None, comm=None):
         cfg.check(world)
+        self.comm = comm
         self.cfg = cfg
         self.rank = rank
         self.world = world
@@ -155,16 +231,24 @@ class TPLayerSet:
         qd = cfg.n_heads * cfg.head_dim // self.world
         f = cfg.ffn // self.world
         lead = self.rank == 0
+        fused = (self.comm is not None and self.world > 1
+                 and self.comm.fits(x.shape[0], cfg.d_model))
         for L in self.layers:
             qkv = ops.rmsnorm_linear(x, L["attn_norm"], L["qkv"], cfg.eps)
             attn = qkv[:, :qd].contiguous()  # attention stand-in (out of scope)
-            x = ops.linear(attn, L["o"], residual=x if lead else None)
-            x = self._all_reduce(x)
+            x = self._row_split(attn, L["o"], x, lead, fused)
             gu = ops.rmsnorm_linear(x, L["ffn_norm"], L["gate_up"], cfg.eps)
             h = ops.swiglu(gu[:, :f].contiguous(), gu[:, f:].contiguous())
-            x = ops.linear(h, L["down"], residual=x if lead else None)
-            x = self._all_reduce(x)
+            x = self._row_split(h, L["down"], x, lead, fused)
         return x
+
+    def _row_split(self, a, W, x, lead, fused):
+        """x + sum over ranks of a_r @ W_r^T (the O / down projection)."""
+        if fused:
+            self.allreduce_count += 1
+            return self.comm.linear_allreduce(a, W, residual=x)
+        y = self.ops.linear(a, W, residual=x if lead else None)
+        return self._all_reduce(y)
 
     def logits_shard(self, x):
         return self.ops.rmsnorm_linear(x, self.final_norm, self.lm_head, self.cfg.eps)
@@ -255,9 +339,14 @@ def bench_main(args, metric: str) -> int:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     cfg = LLAMA3_8B
     layers, lm, embed, fnorm = random_shards(cfg, rank, world, dev)
-    model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm)
     prefill = args.workload == "tp-prefill"
     B = 2048 if prefill else args.batch
+    comm = None
+    collective = "none" if world == 1 else "nccl all_reduce"
+    if world > 1 and not prefill and os.environ.get("ENGINE_TP_COMM", "nvlink") != "nccl":
+        comm = NvlinkComm(rank, world, B * cfg.d_model)
+        collective = "nvlink one-shot all-reduce fused into the O / down projection"
+    model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=comm)
     gen = torch.Generator(device=dev).manual_seed(7)
     ids = torch.randint(0, cfg.vocab, (B,), device=dev, generator=gen, dtype=torch.int32)
     if world > 1:
@@ -308,7 +397,8 @@ def bench_main(args, metric: str) -> int:
         "vs_baseline": None, "dtype": "f16", "data": "synthetic: random N(0,0.02) FP16 weights",
         "config": {"workload": "tp-prefill" if prefill else "tp-decode", "model": "llama3-8b-shaped",
                    "layers": cfg.n_layers, "batch": B, "parallelism": f"tp{world}",
-                   "attention": "stand-in (out of scope)", "cuda_graph": graph is not None},
+                   "attention": "stand-in (out of scope)", "cuda_graph": graph is not None,
+                   "collective": collective},
         "per_gpu_weight_bytes": wbytes,
         "hbm_gbs_per_gpu": (wbytes / (ms * 1e-3) / 1e9) if not prefill else None,
         "tflops_per_gpu": (flops_per_token(cfg) * B / world / (ms * 1e-3) / 1e12),
@@ -317,6 +407,8 @@ def bench_main(args, metric: str) -> int:
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph
+    if comm is not None:
+        comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -342,6 +342,39 @@ def secondary_configs(torch, pkg, dev, g, world, args):
         del X, Y, sets
     del Ws
     torch.cuda.empty_cache()
+    # Config 2: the other two decode GEMV shapes (rotating pools > L2)
+    for (N, K, nsets) in ((4096, 4096, 6), (14336, 4096, 4)):
+        sets = [((torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        fn = lambda s, st, N=N, K=K: pkg.cuda.gemv_f16_nk(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), N, K, st)
+        ms = time_graph(torch, fn, sets, 60, 5)
+        byt = 2.0 * (N * K + K + N)
+        out[f"gemv_{N}x{K}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9}
+        del sets
+    # Config 4a in BF16
+    n = 4096
+    sets = [(torch.randn(n, n, device=dev, generator=g).bfloat16(),
+             torch.randn(n, n, device=dev, generator=g).bfloat16(),
+             torch.empty(n, n, device=dev, dtype=torch.bfloat16)) for _ in range(4)]
+    fn = lambda s, st: pkg.cuda.matmul_bf16(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)
+    ms = time_graph(torch, fn, sets, 20, 3)
+    out["matmul_bf16_4096"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
+    del sets
+    # Config 1: the reference's FP32 register-tiled matmul at 512^3 (48 rotating
+    # 3 MiB sets = 144 MiB > L2)
+    n = 512
+    sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+             torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+             torch.empty(n, n, device=dev)) for _ in range(48)]
+    fn = lambda s, st: pkg.cuda.matmul_register_tiled(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)
+    ms = time_graph(torch, fn, sets, 96, 5)
+    out["matmul_f32_512"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
+    del sets
+    torch.cuda.empty_cache()
     return out
 
 

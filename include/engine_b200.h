@@ -181,6 +181,64 @@ ENGINE_B200_API int engine_cuda_embedding_f16(const engine_half_t* table, const 
                               engine_half_t* out, int64_t num_tokens, int64_t hidden,
                               int64_t vocab, engine_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel communicator over NVLink peer memory.  No counterpart in the
+ * reference (it has no multi-GPU code): these replace the NCCL all-reduce (sum,
+ * FP16) that follows the row-split O and down projections of the
+ * tensor-parallel layer set, and fuse it into the projection for decode.
+ *
+ * One process per GPU.  Set-up, with the rank's device current:
+ *   1. engine_tp_comm_create(rank, world, max_elems, &c)
+ *   2. engine_tp_comm_handle(c, h)     -- ENGINE_TP_HANDLE_BYTES bytes; exchange
+ *      them between the ranks on the host (all-gather)
+ *   3. engine_tp_comm_open(c, all)     -- world x ENGINE_TP_HANDLE_BYTES, rank order
+ *   ... calls ...
+ *   4. a host barrier across the ranks, then engine_tp_comm_destroy(c).
+ * Every rank must make the same sequence of calls, all stream-ordered on one
+ * stream per rank.  Each call waits for the peers on the device with a bounded
+ * wait (ENGINE_WAIT_TIMEOUT_MS); on expiry the kernel sets bit 1 of the device
+ * error word (engine_device_status) and leaves Y unwritten.  Results are
+ * bit-identical on every rank: the sum runs in FP32 in rank order, then the
+ * residual is added and the value is rounded once to FP16.  Calls may be
+ * captured in CUDA graphs; the per-call state lives in device memory.
+ * ------------------------------------------------------------------------- */
+#define ENGINE_TP_HANDLE_BYTES 64
+
+typedef struct engine_tp_comm engine_tp_comm_t;
+
+/* Allocates this rank's exchange region on the current device:
+ * 2 x world x max_elems FP32 slots, flags, call counts.  max_elems bounds the
+ * elements (M*N) of one call.  world <= 8. */
+ENGINE_B200_API int engine_tp_comm_create(int rank, int world, int64_t max_elems,
+                                          engine_tp_comm_t** comm);
+
+/* Copies the region's CUDA IPC handle (ENGINE_TP_HANDLE_BYTES bytes) to `handle`. */
+ENGINE_B200_API int engine_tp_comm_handle(const engine_tp_comm_t* comm, void* handle);
+
+/* Maps every peer's region.  `handles` holds world handles in rank order.  A
+ * handle equal to this rank's own maps to its own region (single-process
+ * loopback). */
+ENGINE_B200_API int engine_tp_comm_open(engine_tp_comm_t* comm, const void* handles);
+
+/* Unmaps the peers and frees the region.  Call after a host barrier. */
+ENGINE_B200_API int engine_tp_comm_destroy(engine_tp_comm_t* comm);
+
+/* y[i] = sum over ranks of partial[i] (+ residual[i]), on every rank. */
+ENGINE_B200_API int engine_tp_allreduce_f16(engine_tp_comm_t* comm, const engine_half_t* partial,
+                                            const engine_half_t* residual, engine_half_t* y,
+                                            int64_t n, engine_stream_t stream);
+
+/* Row-split projection fused with its all-reduce:
+ * Y[M,N] = sum over ranks r of X_r[M,K] * W_r[N,K]^T (+ residual[M,N]) on every rank.
+ * For M <= 4 one kernel streams W_r as the decode GEMV does, pushes its FP32
+ * partial rows to every rank over NVLink and reduces.  Larger M runs the
+ * tensor-core projection, then the one-shot all-reduce. */
+ENGINE_B200_API int engine_tp_linear_allreduce_f16(engine_tp_comm_t* comm, const engine_half_t* X,
+                                                   const engine_half_t* W,
+                                                   const engine_half_t* residual, engine_half_t* Y,
+                                                   int64_t M, int64_t N, int64_t K,
+                                                   engine_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -159,3 +159,18 @@ def test_cpp_adapter_header_compiles():
                         "-I/usr/local/cuda/include", "-x", "c++", "-"], input=src,
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_tp_comm_rejects_bad_arguments(pkg):
+    """engine_tp_*: validation happens before any device work."""
+    c = pkg.cuda
+    _throws(pkg, c.tp_comm_create, 0, 0, 16, substr="world")
+    _throws(pkg, c.tp_comm_create, 0, 9, 16, substr="world")
+    _throws(pkg, c.tp_comm_create, 2, 2, 16, substr="rank")
+    _throws(pkg, c.tp_comm_create, -1, 2, 16, substr="rank")
+    _throws(pkg, c.tp_comm_create, 0, 2, 0, substr="max_elems")
+    _throws(pkg, c.tp_allreduce_f16, 0, P, 0, P, 8, substr="null")
+    _throws(pkg, c.tp_linear_allreduce_f16, 0, P, P, 0, P, 1, 8, 8, substr="null")
+    with pytest.raises(pkg.EngineError):
+        c.tp_comm_handle(0)
+    c.tp_comm_destroy(0)  # destroying nothing is a no-op
