@@ -413,3 +413,100 @@ def bench_main(args, metric: str) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def bench_collectives(args) -> int:
+    """bench.py --workload tp-comm (one process per GPU, world >= 2): device time
+    per call of the row-split projection + all-reduce at the decode shapes,
+    NVLink fused vs GEMV/GEMM + NVLink all-reduce vs GEMV/GEMM + NCCL, and the
+    all-reduces alone.  Each figure is one CUDA graph of 64 back-to-back calls,
+    replayed 5 times, max over ranks."""
+    import datetime
+
+    from . import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world < 2:
+        if rank == 0:
+            print(json.dumps({"workload": "tp-comm", "unavailable": "needs >= 2 GPUs (torchrun)"}))
+        return 0
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = LLAMA3_8B
+    comm = NvlinkComm(rank, world, 32 * cfg.d_model)
+    calls = 64
+
+    def timed(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (5 * calls)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        return float(t.item())
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    out = {}
+    for name, M, K in (("o_b1", 1, cfg.d_model // world), ("down_b1", 1, cfg.ffn // world),
+                       ("down_b32", 32, cfg.ffn // world)):
+        N = cfg.d_model
+        X = torch.randn(M, K, device=dev, generator=gen).half()
+        W = (torch.randn(N, K, device=dev, generator=gen) * 0.02).half()
+        R = torch.randn(M, N, device=dev, generator=gen).half()
+        Y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        P = torch.empty(M, N, device=dev, dtype=torch.float16)
+
+        def nccl_path():
+            ops.linear(X, W, residual=R if rank == 0 else None, out=Y)
+            dist.all_reduce(Y)
+
+        def nv_unfused():
+            ops.linear(X, W, out=P)
+            comm.allreduce(P, residual=R, out=Y)
+
+        out[name] = {
+            "projection_alone_us": timed(lambda: ops.linear(X, W, residual=R, out=Y)),
+            "nvlink_fused_us": timed(lambda: comm.linear_allreduce(X, W, residual=R, out=Y)),
+            "projection_then_nvlink_allreduce_us": timed(nv_unfused),
+            "projection_then_nccl_allreduce_us": timed(nccl_path),
+        }
+    for n in (cfg.d_model, 32 * cfg.d_model):
+        P = torch.randn(n, device=dev, generator=gen).half()
+        Y = torch.empty_like(P)
+        out[f"allreduce_{n * 2 // 1024}KiB"] = {
+            "nvlink_us": timed(lambda: comm.allreduce(P, out=Y)),
+            "nccl_us": timed(lambda: dist.all_reduce(P)),
+        }
+    line = {"metric": "TP row-split projection + all-reduce, device us per call (decode shapes)",
+            "unit": "us", "higher_is_better": False, "n_gpus": world,
+            "config": {"workload": "tp-comm", "model": "llama3-8b-shaped", "parallelism": f"tp{world}",
+                       "timing": f"CUDA graph of {calls} calls x 5 replays, max over ranks"},
+            "results": out}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+

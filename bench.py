@@ -20,7 +20,9 @@ Headline workload (BASELINE metric "FP16 GEMM TFLOP/s (4096^3) & GEMV HBM GB/s
 ``--impl reference`` times the reference's CPU implementation alone (the
 reference has no GPU path for this configuration) and prints its line.
 ``--workload tp-decode|tp-prefill`` runs the Llama-3-8B-shaped tensor-parallel
-projection layer set instead (see bare-metal-llm-engine_b200/tp.py).
+projection layer set instead (see bare-metal-llm-engine_b200/tp.py);
+``--workload tp-comm`` (torchrun, >= 2 GPUs) times the row-split projection with
+its all-reduce: NVLink fused vs NVLink / NCCL after the projection.
 """
 from __future__ import annotations
 
@@ -526,7 +528,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["headline", "tp-decode", "tp-prefill"], default="headline")
+    ap.add_argument("--workload", choices=["headline", "tp-decode", "tp-prefill", "tp-comm"],
+                    default="headline")
     ap.add_argument("--batch", type=int, default=1, help="tp-decode batch (1 or 32)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
@@ -541,6 +544,8 @@ def main() -> int:
         load_pkg()
         from bmle_b200 import tp  # noqa: F811
 
+        if args.workload == "tp-comm":
+            return tp.bench_collectives(args)
         return tp.bench_main(args, METRIC)
     return run_headline(args)
 
