@@ -324,6 +324,11 @@ int engine_device_status(int device, unsigned int* flags) {
     const unsigned int zero = 0;
     e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
   }
+  // A kernel that gave up may have left a stream-K tile half counted.
+  if (e == cudaSuccess && v != 0) {
+    sk_workspace_reset(device);
+    e = cudaDeviceSynchronize();
+  }
   cudaSetDevice(prev);
   if (e != cudaSuccess) return set_cuda_error(e, "engine_device_status");
   *flags = v;

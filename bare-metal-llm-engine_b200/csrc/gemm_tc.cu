@@ -77,8 +77,7 @@ struct TcParams {
   int64_t dp_tiles;             // tiles handed out whole, round-robin over CTA pairs
   int64_t sk_iters;             // k-blocks of the remaining tiles, split evenly over pairs
   float* ws;                    // FP32 partial-tile slots: [pair][2][rank][128 x BN]
-  unsigned long long* ws_cnt;   // arrival counters: [stream-K tile][rank]
-  unsigned int ws_gen;          // launch tag carried in the counters' high word
+  unsigned long long* ws_cnt;   // arrival counters, zero between launches
 #ifdef ENGINE_TC_TRACE
   unsigned long long* trace;  // debug builds: 8 timestamps per CTA
 #endif
@@ -242,27 +241,16 @@ __device__ __forceinline__ int sk_slot_of(const TcParams& p, int64_t q, int64_t 
   return (sk_bound(p, q, npairs) / p.num_kb == tl) ? 0 : 1;
 }
 
-/// Counts this CTA's arrival on a stream-K tile counter and returns the arrival
-/// number (1-based).  The high word carries the launch tag: a count left by an
-/// aborted launch (device time-out) is not mistaken for this launch's.  Release
-/// of this CTA's parked partial and acquire of the other's are both on the CAS.
-__device__ __forceinline__ uint32_t sk_arrive(unsigned long long* cnt, uint32_t gen,
-                                              unsigned int* err) {
+/// Counts this CTA's arrival on a stream-K tile counter; returns the arrival
+/// number (1-based).  acq_rel: releases this CTA's parked partial and acquires
+/// the earlier arrivals'.  The CTA that stores the tile resets the counter to
+/// zero, so every completed launch leaves all counters at zero (CUDA graphs
+/// replay exactly); after a device-side time-out engine_device_status() zeroes
+/// them again.
+__device__ __forceinline__ uint32_t sk_arrive(unsigned long long* cnt) {
   unsigned long long old;
-  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(old) : "l"(cnt) : "memory");
-  for (int tries = 0; tries < 4096; ++tries) {
-    const uint32_t c = (static_cast<uint32_t>(old >> 32) == gen) ? static_cast<uint32_t>(old) + 1 : 1u;
-    const unsigned long long nv = (static_cast<unsigned long long>(gen) << 32) | c;
-    unsigned long long prev;
-    asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;"
-                 : "=l"(prev)
-                 : "l"(cnt), "l"(old), "l"(nv)
-                 : "memory");
-    if (prev == old) return c;
-    old = prev;
-  }
-  atomicOr(err, kErrWaitTimeout);  // a CAS that never wins: report, do not loop on
-  return 0;
+  asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(cnt) : "memory");
+  return static_cast<uint32_t>(old) + 1u;
 }
 
 __device__ __forceinline__ void sk_reset(unsigned long long* cnt) {
@@ -915,7 +903,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (warp == 2 && lane == 0) {
           unsigned long long v;
           asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(cnt) : "memory");
-          const bool second = static_cast<uint32_t>(v >> 32) == p.ws_gen && static_cast<uint32_t>(v) == 1u;
+          const bool second = static_cast<uint32_t>(v) == 1u;
           if (second) sk_reset(cnt);
           *sk_flag = second ? 1u : 0u;
         }
@@ -936,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           named_barrier_sync(1, 128);
           if (warp == 2 && lane == 0) {
-            const uint32_t n = sk_arrive(cnt, p.ws_gen, p.err);
+            const uint32_t n = sk_arrive(cnt);
             if (n == 2) sk_reset(cnt);
             *sk_flag = (n == 2) ? 1u : 0u;
           }
@@ -1154,29 +1142,34 @@ int env_int(const char* name, int dflt) {
 }
 
 // Stream-K workspace of the 2-SM kernel, one per (device, stream): calls on one
-// stream run one after another, so their partial slots and counters never
-// overlap; calls on different streams get different workspaces.  Sized for the
-// largest grid (one pair slot pair per 2 SMs, BN = 256) and kept for the life of
-// the process.  Counters start at zero and every completed launch leaves them
-// at zero, so a CUDA graph may replay a captured launch.  The first call on a
+// stream run one after another (every access follows the kernel's
+// griddepcontrol.wait), so their partial slots and counters never overlap;
+// calls on different streams get different workspaces.  Sized for the largest
+// grid (two slots per CTA pair, BN = 256) and kept for the life of the
+// process.  Counters start at zero and every completed launch leaves them at
+// zero, so a CUDA graph may replay a captured launch.  The first call on a
 // stream allocates; a call made during stream capture before that falls back
 // to whole-tile scheduling.
 struct SkWorkspace {
   float* parts = nullptr;
   unsigned long long* cnt = nullptr;
-  unsigned int gen = 0;
+  size_t cnt_bytes = 0;
 };
 
+std::mutex g_sk_mu;
+std::map<std::pair<int, cudaStream_t>, SkWorkspace> g_sk_spaces;
+
 bool sk_workspace(int dev, cudaStream_t stream, int max_pairs, float** parts,
-                  unsigned long long** cnt, unsigned int* gen) {
-  static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, SkWorkspace> spaces;
-  std::lock_guard<std::mutex> lk(mu);
+                  unsigned long long** cnt) {
+  std::lock_guard<std::mutex> lk(g_sk_mu);
+  auto& spaces = g_sk_spaces;
   SkWorkspace& w = spaces[std::make_pair(dev, stream)];
   if (w.parts == nullptr) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
       return false;
+    // Partial slots: 2 per pair x 2 CTAs x 128 x 256 FP32.  Counters: one per
+    // (stream-K tile, CTA rank); the stream-K region has fewer than 2 x pairs tiles.
     const size_t part_bytes = static_cast<size_t>(max_pairs) * 2 * 2 * 128 * 256 * sizeof(float);
     const size_t cnt_bytes = static_cast<size_t>(2 * max_pairs) * 2 * sizeof(unsigned long long);
     void* mem = nullptr;
@@ -1191,11 +1184,10 @@ bool sk_workspace(int dev, cudaStream_t stream, int max_pairs, float** parts,
     }
     w.parts = reinterpret_cast<float*>(mem);
     w.cnt = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(mem) + part_bytes);
+    w.cnt_bytes = cnt_bytes;
   }
-  if (++w.gen == 0) w.gen = 1;  // 0 never tags a live count
   *parts = w.parts;
   *cnt = w.cnt;
-  *gen = w.gen;
   return true;
 }
 
@@ -1246,6 +1238,14 @@ int gemm_tc(const void* A, const void* B, const void* residual, void* C, int64_t
 int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C, int64_t M,
                      int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
                      cudaStream_t stream);
+
+void sk_workspace_reset(int dev) {
+  std::lock_guard<std::mutex> lk(g_sk_mu);
+  for (auto& kv : g_sk_spaces) {
+    if (kv.first.first == dev && kv.second.cnt != nullptr)
+      cudaMemset(kv.second.cnt, 0, kv.second.cnt_bytes);
+  }
+}
 
 int gemm_tc_general(const void* A, const void* B, const void* residual, void* C, int64_t M,
                     int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
@@ -1404,7 +1404,7 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
         p.num_kb >= 8) {
       int dev = 0;
       B200_CUDA(cudaGetDevice(&dev));
-      if (sk_workspace(dev, stream, sms / 2, &p.ws, &p.ws_cnt, &p.ws_gen)) {
+      if (sk_workspace(dev, stream, sms / 2, &p.ws, &p.ws_cnt)) {
         p.dp_tiles = (waves - 1) * pairs;
         p.sk_iters = (tiles - p.dp_tiles) * p.num_kb;
       }

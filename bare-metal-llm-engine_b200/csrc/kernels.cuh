@@ -57,4 +57,9 @@ int rmsnorm_hilo(const __half* x, const __half* gamma, __half* out, int64_t M, i
 void* scratch_alloc(size_t bytes, cudaStream_t stream);
 void scratch_free(void* p, cudaStream_t stream);
 
+/// Zeroes the stream-K tile counters of every workspace on `dev` (after a
+/// device-side time-out may have left a launch half counted).  The device must
+/// be idle.  gemm_tc.cu.
+void sk_workspace_reset(int dev);
+
 }  // namespace b200
