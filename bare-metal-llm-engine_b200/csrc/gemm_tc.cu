@@ -1065,30 +1065,6 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (q.split <= 0) {
-    // Automatic split-K (SWAP tiles): the largest cluster size S <= q.kb_per_split
-    // (the caller's cap) whose clusters are ALL co-resident, so no cluster waits
-    // for a second wave.  Occupancy per (device, S) is queried once and cached.
-    static std::atomic<int> fits[64][9];
-    const int cap = q.kb_per_split > 8 ? 8 : static_cast<int>(q.kb_per_split);
-    int best = 1;
-    for (int S = cap; S >= 2; --S) {
-      int n = fits[dev & 63][S].load();
-      if (n == 0) {
-        cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(S));
-        attr[0].val.clusterDim.z = static_cast<unsigned>(S);
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = -1;
-        cudaGetLastError();
-        fits[dev & 63][S].store(n == 0 ? -1 : n);
-      }
-      if (n >= grid_x) {
-        best = S;
-        break;
-      }
-    }
-    q.split = best;
-    q.kb_per_split = (q.num_kb + best - 1) / best;
-  }
   cfg.gridDim = dim3(static_cast<unsigned>(grid_x), 1, static_cast<unsigned>(q.split));
   attr[0].val.clusterDim.z = static_cast<unsigned>(q.split);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
@@ -1327,28 +1303,24 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
     p.tiles_n = 1;
     p.half_b = half_b;
     const int tiles = p.tiles_m;
-    // Split-K over a cluster when the weight tiles alone cannot cover the SMs
-    // (two CTAs fit per SM in this mode); launch_tc picks the cluster size from
-    // occupancy, capped here at 8 and at four k-blocks per split.
-    int cap = 1;
-    if (tiles < 2 * sms) {
-      cap = (2 * sms) / tiles;
-      if (cap > 8) cap = 8;
+    // Split-K over a cluster of S CTAs when the weight tiles alone cannot cover
+    // the SMs (two CTAs fit per SM in this mode): the largest S <= 8 with at
+    // least four k-blocks per split and tiles x S within 85% of the 2-per-SM
+    // slots.  A B200 sweep (M = 16; N x K = 6144x4096, 4096x4096, 28672x4096,
+    // 4096x14336) found that point fastest on every shape.  Clusters that do
+    // not all fit at once only wait for a slot: no cluster depends on another.
+    int S = 1;
+    if (tiles > 0) {
+      S = static_cast<int>((static_cast<int64_t>(sms) * 2 * 85 / 100) / tiles);
+      if (S > 8) S = 8;
       const int64_t kmax = p.num_kb / 4;
-      if (cap > kmax) cap = static_cast<int>(kmax > 0 ? kmax : 1);
-      if (cap < 1) cap = 1;
+      if (S > kmax) S = static_cast<int>(kmax);
+      if (S < 1) S = 1;
     }
     static const int split_env = env_int("ENGINE_TC_SPLIT", 0);
-    if (split_env > 0) {
-      p.split = split_env > 8 ? 8 : split_env;
-      p.kb_per_split = (p.num_kb + p.split - 1) / p.split;
-    } else if (cap > 1) {
-      p.split = 0;              // automatic
-      p.kb_per_split = cap;     // the cap, consumed by launch_tc
-    } else {
-      p.split = 1;
-      p.kb_per_split = p.num_kb;
-    }
+    if (split_env > 0) S = split_env > 8 ? 8 : split_env;
+    p.split = S;
+    p.kb_per_split = (p.num_kb + S - 1) / S;
     const int grid = tiles;
     if (hilo) {
       switch (bn) {

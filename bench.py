@@ -376,6 +376,16 @@ def secondary_configs(torch, pkg, dev, g, world, args):
     ms = time_graph(torch, fn, sets, 96, 5)
     out["matmul_f32_512"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
     del sets
+    # The reference's own headline size for the FP32 register-tiled matmul, 4096^3
+    # (2 rotating sets of 192 MiB > L2)
+    n = 4096
+    sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+             torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+             torch.empty(n, n, device=dev)) for _ in range(2)]
+    ms = time_graph(torch, fn_f32 := (lambda s, st: pkg.cuda.matmul_register_tiled(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)), sets, 4, 3)
+    out["matmul_f32_4096"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
+    del sets, fn_f32
     torch.cuda.empty_cache()
     return out
 
