@@ -72,16 +72,19 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
   }
 }
 
-// Batch-1 fused RMSNorm -> GEMV.  Each CTA first issues the loads of its first
-// weight chunks, then forms t = x * gamma (FP32) in shared memory and the sum of
-// squares of x with a block reduction -- once per CTA instead of once per warp
-// and chunk -- and streams W against t.  The RMS scale multiplies the finished
-// dot product: y = scale * sum_k t_k W_nk (+ residual).
+// Batch-1 fused RMSNorm -> GEMV.  Persistent: each CTA forms t = x * gamma
+// (FP32) in shared memory and the sum of squares of x with one block reduction
+// -- once per CTA, not once per row block -- then streams row block after row
+// block (blockIdx.x, + gridDim.x, ...) against t.  The RMS scale multiplies each
+// finished dot product: y = scale * sum_k t_k W_nk (+ residual).  The first row
+// block's first weight chunks are prefetched into L2 before griddepcontrol.wait
+// and loaded before the prologue, so HBM is busy while t is formed.
 template <int RPW, int SK, int U, bool RESID>
 __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
     const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
     const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps) {
   constexpr int GROUPS = kNkVecWarps / SK;
+  constexpr int64_t ROWS = static_cast<int64_t>(GROUPS) * RPW;
   extern __shared__ __align__(16) float s_t[];  // K floats
   __shared__ float red[kNkVecWarps][RPW];
   __shared__ float s_ss[kNkVecWarps];
@@ -89,17 +92,20 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
   const int warp = threadIdx.x >> 5;
   const int grp = warp / SK;
   const int sub = warp % SK;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * GROUPS + grp) * RPW;
   const int64_t nchunk = K >> 3;
+  const int64_t nblocks = (N + ROWS - 1) / ROWS;
   constexpr int64_t kStride = 32 * SK;
-  const bool active = row0 < N;
 
   const __half* wrow[RPW];
+  auto set_rows = [&](int64_t b) {
+    const int64_t row0 = (b * GROUPS + grp) * RPW;
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    const int64_t n = (row0 + r < N) ? row0 + r : N - 1;
-    wrow[r] = W + n * K;
-  }
+    for (int r = 0; r < RPW; ++r) {
+      const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: never stored
+      wrow[r] = W + n * K;
+    }
+    return row0 < N;
+  };
   uint4 wa[U][RPW], wb[U][RPW];
   auto load = [&](int64_t c0, uint4 (&w)[U][RPW]) {
 #pragma unroll
@@ -111,12 +117,13 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
       }
     }
   };
-  int64_t c0 = sub * 32 + lane;
+  const int64_t cstart = sub * 32 + lane;
+  bool active = set_rows(blockIdx.x);
   pdl_trigger();
   if (active) {  // warm L2 with the first weight chunks while the preceding kernel drains
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t c = c0 + kStride * u;
+      const int64_t c = cstart + kStride * u;
       if (c < nchunk) {
 #pragma unroll
         for (int r = 0; r < RPW; ++r) prefetch_l2(wrow[r] + 8 * c);
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
     }
   }
   pdl_wait();
-  if (active) load(c0, wa);
+  if (active) load(cstart, wa);
 
   // Prologue: t = x * gamma into shared memory, sum of squares of x.
   float ss = 0.0f;
@@ -142,71 +149,79 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
       ss = fmaf(xf[i], xf[i], ss);
       xf[i] *= gf[i];
     }
-    float4* dst = reinterpret_cast<float4*>(s_t + 8 * k8);
-    dst[0] = make_float4(xf[0], xf[1], xf[2], xf[3]);
-    dst[1] = make_float4(xf[4], xf[5], xf[6], xf[7]);
+    // Two planes (elements 0-3 and 4-7 of each 8-element chunk): the lanes of a
+    // warp then read 16-byte words at a 16-byte stride, free of bank conflicts.
+    *reinterpret_cast<float4*>(s_t + 4 * k8) = make_float4(xf[0], xf[1], xf[2], xf[3]);
+    *reinterpret_cast<float4*>(s_t + 4 * (nchunk + k8)) = make_float4(xf[4], xf[5], xf[6], xf[7]);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (lane == 0) s_ss[warp] = ss;
-  __syncthreads();
-
-  float acc[RPW];
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
-  auto compute = [&](int64_t cc, uint4 (&w)[U][RPW]) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t c = cc + kStride * u;
-      if (c < nchunk) {
-        const float4 t0 = *reinterpret_cast<const float4*>(s_t + 8 * c);
-        const float4 t1 = *reinterpret_cast<const float4*>(s_t + 8 * c + 4);
-        const float tf[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          float wf[8];
-          h8_to_f8(w[u][r], wf);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[r] = fmaf(tf[i], wf[i], acc[r]);
-        }
-      }
-    }
-  };
-  if (active) {
-    for (; c0 < nchunk; c0 += 2 * kStride * U) {
-      const int64_t c1 = c0 + kStride * U;
-      load(c1, wb);
-      compute(c0, wa);
-      load(c1 + kStride * U, wa);
-      compute(c1, wb);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) red[warp][r] = acc[r];
-  }
   __syncthreads();
   float total = 0.0f;
 #pragma unroll
   for (int w = 0; w < kNkVecWarps; ++w) total += s_ss[w];
   const float scale = static_cast<float>(
       1.0 / sqrt(static_cast<double>(total) / static_cast<double>(K) + static_cast<double>(eps)));
-  for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
-    const int g = o / RPW;
-    const int r = o % RPW;
-    const int64_t row = (static_cast<int64_t>(blockIdx.x) * GROUPS + g) * RPW + r;
-    if (row >= N) continue;
-    float v = 0.0f;
+
+  for (int64_t b = blockIdx.x; b < nblocks; b += gridDim.x) {
+    if (b != blockIdx.x) {
+      active = set_rows(b);
+      if (active) load(cstart, wa);
+    }
+    float acc[RPW];
 #pragma unroll
-    for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
-    v = v * scale;
-    if constexpr (RESID) v = v + __half2float(R[row]);
-    Y[row] = __float2half_rn(v);
+    for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+    auto compute = [&](int64_t cc, uint4 (&w)[U][RPW]) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = cc + kStride * u;
+        if (c < nchunk) {
+          const float4 t0 = *reinterpret_cast<const float4*>(s_t + 4 * c);
+          const float4 t1 = *reinterpret_cast<const float4*>(s_t + 4 * (nchunk + c));
+          const float tf[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+          for (int r = 0; r < RPW; ++r) {
+            float wf[8];
+            h8_to_f8(w[u][r], wf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[r] = fmaf(tf[i], wf[i], acc[r]);
+          }
+        }
+      }
+    };
+    if (active) {
+      for (int64_t c0 = cstart; c0 < nchunk; c0 += 2 * kStride * U) {
+        const int64_t c1 = c0 + kStride * U;
+        load(c1, wb);
+        compute(c0, wa);
+        load(c1 + kStride * U, wa);
+        compute(c1, wb);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) red[warp][r] = acc[r];
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
+      const int g = o / RPW;
+      const int r = o % RPW;
+      const int64_t row = (b * GROUPS + g) * RPW + r;
+      if (row >= N) continue;
+      float v = 0.0f;
+#pragma unroll
+      for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
+      v = v * scale;
+      if constexpr (RESID) v = v + __half2float(R[row]);
+      Y[row] = __float2half_rn(v);
+    }
+    __syncthreads();  // `red` is reused by the next row block
   }
 }
 
@@ -265,13 +280,13 @@ template <int RPW, int SK, bool RESID>
 int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const __half* R,
                     __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
   constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * RPW;
-  const unsigned grid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
+  const int64_t nblocks = (N + rows_per_cta - 1) / rows_per_cta;
   const size_t smem = static_cast<size_t>(K) * sizeof(float);
   auto kern = gemv_nk_norm1_kernel<RPW, SK, 4, RESID>;
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev));
   if (smem > 48 * 1024) {  // opt in once per device to the largest size the dispatch allows
     static std::atomic<uint64_t> configured{0};
-    int dev = 0;
-    B200_CUDA(cudaGetDevice(&dev));
     const uint64_t bit = 1ull << (dev & 63);
     if ((configured.load() & bit) == 0) {
       B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -279,6 +294,13 @@ int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const
       configured.fetch_or(bit);
     }
   }
+  // Persistent grid: as many CTAs as are resident at once (the prologue runs
+  // once per CTA), never more than there are row blocks.
+  int per_sm = 0;
+  B200_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNkVecWarps * 32, smem));
+  if (per_sm < 1) per_sm = 1;
+  const int64_t resident = static_cast<int64_t>(per_sm) * sm_count();
+  const unsigned grid = static_cast<unsigned>(nblocks < resident ? nblocks : resident);
   B200_CUDA(launch_pdl(kern, dim3(grid), dim3(kNkVecWarps * 32), smem, stream, W, X, gamma, R, Y,
                        N, K, eps));
   return ENGINE_OK;
