@@ -57,6 +57,7 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_rmsnorm_linear_f16": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_rmsnorm_linear_f16_noalloc": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_swiglu_f16": [_p, _p, _p, _i64, _p],
+    "engine_cuda_rmsnorm_linear_swiglu_f16": [_p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_embedding_f16": [_p, _p, _p, _i64, _i64, _i64, _p],
     "engine_tp_comm_create": [ctypes.c_int, ctypes.c_int, _i64, ctypes.POINTER(ctypes.c_void_p)],
     "engine_tp_comm_handle": [_p, _p],

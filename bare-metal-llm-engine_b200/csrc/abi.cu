@@ -271,10 +271,7 @@ __global__ void swiglu_f16_kernel(const __half* __restrict__ g, const __half* __
   pdl_wait();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float gv = __half2float(g[i]);
-    const float uv = __half2float(u[i]);
-    const float silu = gv / (1.0f + expf(-gv));
-    out[i] = __float2half_rn(silu * uv);
+    out[i] = swiglu_h(g[i], u[i]);
   }
 }
 

@@ -137,6 +137,15 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+/// SwiGLU of one FP16 gate / up pair: silu(g) * u in float with the library
+/// expf, rounded once to FP16.  The standalone swiglu kernel and the fused
+/// gate/up projection use this one definition, so they agree bit for bit.
+__device__ __forceinline__ __half swiglu_h(__half g, __half u) {
+  const float gv = __half2float(g);
+  const float silu = gv / (1.0f + expf(-gv));
+  return __float2half_rn(silu * __half2float(u));
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -79,12 +79,17 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
 // finished dot product: y = scale * sum_k t_k W_nk (+ residual).  The first row
 // block's first weight chunks are prefetched into L2 before griddepcontrol.wait
 // and loaded before the prologue, so HBM is busy while t is formed.
-template <int RPW, int SK, int U, bool RESID>
+//
+// PAIR (the SwiGLU projection): W holds 2N rows, gate rows [0, N) then up rows
+// [N, 2N).  Warp group j streams the pair (j, N + j) -- each row accumulated
+// exactly as without PAIR -- and writes swiglu(fp16(gate_j), fp16(up_j)).
+template <int RPW, int SK, int U, bool RESID, bool PAIR = false>
 __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
     const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
     const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps) {
   constexpr int GROUPS = kNkVecWarps / SK;
-  constexpr int64_t ROWS = static_cast<int64_t>(GROUPS) * RPW;
+  static_assert(!PAIR || (RPW == 2 && !RESID), "PAIR streams one gate/up row pair per group");
+  constexpr int64_t ROWS = static_cast<int64_t>(GROUPS) * (PAIR ? 1 : RPW);  // outputs per block
   extern __shared__ __align__(16) float s_t[];  // K floats
   __shared__ float red[kNkVecWarps][RPW];
   __shared__ float s_ss[kNkVecWarps];
@@ -98,13 +103,21 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
 
   const __half* wrow[RPW];
   auto set_rows = [&](int64_t b) {
-    const int64_t row0 = (b * GROUPS + grp) * RPW;
+    if constexpr (PAIR) {
+      const int64_t j = b * GROUPS + grp;
+      const int64_t jc = (j < N) ? j : N - 1;  // clamp: never stored
+      wrow[0] = W + jc * K;
+      wrow[1] = W + (N + jc) * K;
+      return j < N;
+    } else {
+      const int64_t row0 = (b * GROUPS + grp) * RPW;
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: never stored
-      wrow[r] = W + n * K;
+      for (int r = 0; r < RPW; ++r) {
+        const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamp: never stored
+        wrow[r] = W + n * K;
+      }
+      return row0 < N;
     }
-    return row0 < N;
   };
   uint4 wa[U][RPW], wb[U][RPW];
   auto load = [&](int64_t c0, uint4 (&w)[U][RPW]) {
@@ -209,17 +222,31 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
       for (int r = 0; r < RPW; ++r) red[warp][r] = acc[r];
     }
     __syncthreads();
-    for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
-      const int g = o / RPW;
-      const int r = o % RPW;
-      const int64_t row = (b * GROUPS + g) * RPW + r;
-      if (row >= N) continue;
-      float v = 0.0f;
+    if constexpr (PAIR) {
+      for (int o = threadIdx.x; o < GROUPS; o += blockDim.x) {
+        const int64_t j = b * GROUPS + o;
+        if (j >= N) continue;
+        float vg = 0.0f, vu = 0.0f;
 #pragma unroll
-      for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
-      v = v * scale;
-      if constexpr (RESID) v = v + __half2float(R[row]);
-      Y[row] = __float2half_rn(v);
+        for (int q = 0; q < SK; ++q) {
+          vg += red[o * SK + q][0];
+          vu += red[o * SK + q][1];
+        }
+        Y[j] = swiglu_h(__float2half_rn(vg * scale), __float2half_rn(vu * scale));
+      }
+    } else {
+      for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
+        const int g = o / RPW;
+        const int r = o % RPW;
+        const int64_t row = (b * GROUPS + g) * RPW + r;
+        if (row >= N) continue;
+        float v = 0.0f;
+#pragma unroll
+        for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
+        v = v * scale;
+        if constexpr (RESID) v = v + __half2float(R[row]);
+        Y[row] = __float2half_rn(v);
+      }
     }
     __syncthreads();  // `red` is reused by the next row block
   }
@@ -276,13 +303,13 @@ void launch_nk_vec(const __half* W, const __half* X, const __half* gamma, const 
              0, stream, W, X, gamma, R, Y, N, K, eps);
 }
 
-template <int RPW, int SK, bool RESID>
+template <int RPW, int SK, bool RESID, bool PAIR = false>
 int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const __half* R,
                     __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
-  constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * RPW;
+  constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * (PAIR ? 1 : RPW);
   const int64_t nblocks = (N + rows_per_cta - 1) / rows_per_cta;
   const size_t smem = static_cast<size_t>(K) * sizeof(float);
-  auto kern = gemv_nk_norm1_kernel<RPW, SK, 4, RESID>;
+  auto kern = gemv_nk_norm1_kernel<RPW, SK, 4, RESID, PAIR>;
   int dev = 0;
   B200_CUDA(cudaGetDevice(&dev));
   if (smem > 48 * 1024) {  // opt in once per device to the largest size the dispatch allows
@@ -584,6 +611,23 @@ int gemv_nk_f16(const __half* W, const __half* X, const __half* gamma, float eps
     }
   }
   return check_launch("gemv_f16_nk");
+}
+
+int gemv_nk_norm1_swiglu_f16(const __half* W, const __half* X, const __half* gamma, float eps,
+                             __half* Y, int64_t F, int64_t K, cudaStream_t stream) {
+  const bool vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(W) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(X) % 16 == 0) &&
+                   (gamma == nullptr || reinterpret_cast<uintptr_t>(gamma) % 16 == 0);
+  static const int norm1_env = env_int("ENGINE_GEMV_NORM1", 1);
+  if (!vec || K > 40960 || norm1_env == 0) return ENGINE_ERR_UNSUPPORTED;
+  // Same warps per row as the unfused batch-1 norm GEMV, so each gate / up row
+  // is accumulated identically.
+  static const int sk_env = env_int("ENGINE_GEMV_SK", 0);
+  const int rc = (sk_env == 1)
+                     ? launch_nk_norm1<2, 1, false, true>(W, X, gamma, nullptr, Y, F, K, eps, stream)
+                     : launch_nk_norm1<2, 2, false, true>(W, X, gamma, nullptr, Y, F, K, eps, stream);
+  if (rc != ENGINE_OK) return rc;
+  return check_launch("rmsnorm_linear_swiglu_f16 (batch-1 GEMV)");
 }
 
 int gemv_kn_f32(const float* A, const float* x, float* out, int64_t N, int64_t K,

@@ -57,6 +57,13 @@ int rmsnorm_hilo(const __half* x, const __half* gamma, __half* out, int64_t M, i
 void* scratch_alloc(size_t bytes, cudaStream_t stream);
 void scratch_free(void* p, cudaStream_t stream);
 
+/// Batch-1 RMSNorm -> gate/up projection with the SwiGLU in its epilogue:
+/// Y[F] = swiglu(rmsnorm(x) W[0:F]^T, rmsnorm(x) W[F:2F]^T).  Returns
+/// ENGINE_ERR_UNSUPPORTED (nothing launched) when the shape / alignment does not
+/// fit the fused kernel.  gemv.cu.
+int gemv_nk_norm1_swiglu_f16(const __half* W, const __half* X, const __half* gamma, float eps,
+                             __half* Y, int64_t F, int64_t K, cudaStream_t stream);
+
 /// Zeroes the stream-K tile counters of every workspace on `dev` (after a
 /// device-side time-out may have left a launch half counted).  The device must
 /// be idle.  gemm_tc.cu.

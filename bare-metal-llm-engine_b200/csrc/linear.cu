@@ -81,6 +81,20 @@ __global__ void __launch_bounds__(256) rmsnorm_hilo_kernel(const __half* __restr
   }
 }
 
+// Y[m, i] = swiglu(GU[m, i], GU[m, F + i]) over the [M, 2F] gate/up rows.
+__global__ void swiglu_rows_kernel(const __half* __restrict__ gu, __half* __restrict__ y,
+                                   int64_t M, int64_t F) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t n = M * F;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / F;
+    const int64_t c = i - m * F;
+    y[i] = swiglu_h(gu[m * 2 * F + c], gu[m * 2 * F + F + c]);
+  }
+}
+
 int linear_impl(const void* X, const void* W, const void* R, void* Y, int64_t M, int64_t N,
                 int64_t K, bool bf16, cudaStream_t stream) {
   if (!bf16 && M <= 4) {
@@ -228,3 +242,48 @@ int engine_cuda_rmsnorm_linear_f16(const engine_half_t* x, const engine_half_t* 
 }
 
 }  // extern "C"
+
+extern "C" int engine_cuda_rmsnorm_linear_swiglu_f16(const engine_half_t* x,
+                                                     const engine_half_t* gamma,
+                                                     const engine_half_t* W_gu, engine_half_t* Y,
+                                                     int64_t M, int64_t F, int64_t K, float eps,
+                                                     engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(M >= 0 && F >= 0 && K >= 0, "rmsnorm_linear_swiglu_f16: negative dimension");
+  B200_REQUIRE(x != nullptr && W_gu != nullptr && Y != nullptr,
+               "rmsnorm_linear_swiglu_f16: null device pointer");
+  B200_REQUIRE(eps >= 0.0f, "rmsnorm_linear_swiglu_f16: eps must be non-negative");
+  if (M == 0 || F == 0) return ENGINE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {  // empty projections: swiglu(0, 0) = 0
+    B200_CUDA(cudaMemsetAsync(Y, 0, static_cast<size_t>(M * F) * sizeof(engine_half_t), st));
+    return ENGINE_OK;
+  }
+  const __half* xh = reinterpret_cast<const __half*>(x);
+  const __half* gh = reinterpret_cast<const __half*>(gamma);
+  const __half* wh = reinterpret_cast<const __half*>(W_gu);
+  __half* yh = reinterpret_cast<__half*>(Y);
+  if (M == 1) {
+    const int rc = gemv_nk_norm1_swiglu_f16(wh, xh, gh, eps, yh, F, K, st);
+    if (rc != ENGINE_ERR_UNSUPPORTED) return rc;
+  }
+  // Otherwise: the projection into stream-ordered scratch, then the SwiGLU.
+  const size_t bytes = static_cast<size_t>(M) * static_cast<size_t>(2 * F) * sizeof(__half);
+  __half* gu = static_cast<__half*>(scratch_alloc(bytes, st));
+  if (gu == nullptr) return ENGINE_ERR_CUDA;
+  int rc = engine_cuda_rmsnorm_linear_f16(x, gamma, W_gu, nullptr,
+                                          reinterpret_cast<engine_half_t*>(gu), M, 2 * F, K, eps,
+                                          stream);
+  if (rc == ENGINE_OK) {
+    const int64_t n = M * F;
+    const int64_t blocks64 = (n + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(blocks64 < 4096 ? blocks64 : 4096);
+    const cudaError_t e =
+        launch_pdl(swiglu_rows_kernel, dim3(blocks), dim3(256), 0, st, gu, yh, M, F);
+    rc = (e == cudaSuccess) ? check_launch("rmsnorm_linear_swiglu_f16")
+                            : set_cuda_error(e, "rmsnorm_linear_swiglu_f16");
+  }
+  scratch_free(gu, st);
+  return rc;
+  B200_ENTRY_END
+}

@@ -87,6 +87,12 @@ def rmsnorm_linear_f16(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
                                                 _s(stream)))
 
 
+def rmsnorm_linear_swiglu_f16(x, gamma, W_gu, Y, M, F, K, eps, stream=0):
+    """Y[M,F] = swiglu(rmsnorm(x) W_gu[0:F]^T, rmsnorm(x) W_gu[F:2F]^T) in one call
+    (kernels.hpp rmsnorm_linear followed by swiglu_fp16)."""
+    _check(lib().engine_cuda_rmsnorm_linear_swiglu_f16(x, gamma, W_gu, Y, M, F, K, eps, _s(stream)))
+
+
 def rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
     """rmsnorm_linear_f16 without any device allocation (fixed in-library scratch;
     M <= 32, K <= 16384).  Concurrent calls on unordered streams race."""

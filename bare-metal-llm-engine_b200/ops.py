@@ -100,6 +100,21 @@ def rmsnorm_linear(x, gamma, W, eps: float = 1e-5, residual=None, out=None):
     return Y
 
 
+def rmsnorm_linear_swiglu(x, gamma, W_gu, eps: float = 1e-5, out=None):
+    """swiglu(g, u) with [g | u] = rmsnorm(x; gamma, eps) @ W_gu^T, W_gu [2F,K] = gate
+    rows then up rows; FP16.  Same result as rmsnorm_linear followed by swiglu."""
+    _req(x, torch.float16, "x")
+    _req(W_gu, torch.float16, "W_gu")
+    if gamma is not None:
+        _req(gamma, torch.float16, "gamma")
+    M, K = x.shape
+    F = W_gu.shape[0] // 2
+    Y = out if out is not None else torch.empty(M, F, device=x.device, dtype=torch.float16)
+    _c.rmsnorm_linear_swiglu_f16(x.data_ptr(), _ptr(gamma), W_gu.data_ptr(), Y.data_ptr(), M, F,
+                                 K, eps, _stream())
+    return Y
+
+
 def swiglu(gate, up, out=None):
     _req(gate, torch.float16, "gate")
     _req(up, torch.float16, "up")

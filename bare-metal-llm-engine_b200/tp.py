@@ -15,7 +15,8 @@ style over t ranks:
   tiny all-gather of (value, index) pairs.
 
 Per layer: x -> rmsnorm_linear(QKV) -> [attention stand-in] -> linear(O) ->
-all-reduce -> rmsnorm_linear(gate/up) -> swiglu -> linear(down) -> all-reduce.
+all-reduce -> rmsnorm_linear_swiglu(gate/up, SwiGLU fused) -> linear(down) ->
+all-reduce.
 The residual add is folded into rank 0's O / down epilogue, so the all-reduced
 sum is already x + sum_r proj_r.  Attention itself is out of scope for this
 hot path: the stand-in passes each rank's q-head slice straight to O, which
@@ -124,6 +125,9 @@ class CudaOps:
     def swiglu(self, g, u, out=None):
         return self._o.swiglu(g, u, out=out)
 
+    def rmsnorm_linear_swiglu(self, x, gamma, W_gu, eps, out=None):
+        return self._o.rmsnorm_linear_swiglu(x, gamma, W_gu, eps, out=out)
+
     def embedding(self, table, ids, out=None):
         return self._o.embedding(table, ids, out=out)
 
@@ -229,7 +233,6 @@ class TPLayerSet:
         """Runs every layer on the replicated residual stream x [B, d_model]."""
         cfg, ops = self.cfg, self.ops
         qd = cfg.n_heads * cfg.head_dim // self.world
-        f = cfg.ffn // self.world
         lead = self.rank == 0
         fused = (self.comm is not None and self.world > 1
                  and self.comm.fits(x.shape[0], cfg.d_model))
@@ -237,8 +240,8 @@ class TPLayerSet:
             qkv = ops.rmsnorm_linear(x, L["attn_norm"], L["qkv"], cfg.eps)
             attn = qkv[:, :qd].contiguous()  # attention stand-in (out of scope)
             x = self._row_split(attn, L["o"], x, lead, fused)
-            gu = ops.rmsnorm_linear(x, L["ffn_norm"], L["gate_up"], cfg.eps)
-            h = ops.swiglu(gu[:, :f].contiguous(), gu[:, f:].contiguous())
+            # gate/up projection with the SwiGLU fused (one kernel at batch 1)
+            h = ops.rmsnorm_linear_swiglu(x, L["ffn_norm"], L["gate_up"], cfg.eps)
             x = self._row_split(h, L["down"], x, lead, fused)
         return x
 

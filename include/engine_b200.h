@@ -169,6 +169,21 @@ ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16_noalloc(
     const engine_half_t* residual, engine_half_t* Y, int64_t M, int64_t N, int64_t K, float eps,
     engine_stream_t stream);
 
+/* Fused RMSNorm -> gate/up projection -> SwiGLU.  No single reference
+ * counterpart: it is kernels.hpp:97 (rmsnorm_linear, FP16 [N,K] form) followed by
+ * kernels.hpp:141 (swiglu_fp16), in one call.  W_gu[2F,K] holds the gate rows
+ * [0, F) then the up rows [F, 2F) (the tensor-parallel shard layout);
+ * Y[M,F] = swiglu(g, u) with g, u the FP16 projections -- bit-identical to
+ * engine_cuda_rmsnorm_linear_f16 into [M,2F] followed by engine_cuda_swiglu_f16.
+ * Batch 1 is one kernel that never writes g and u; larger batches use a
+ * stream-ordered scratch for them. */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear_swiglu_f16(const engine_half_t* x,
+                                                          const engine_half_t* gamma,
+                                                          const engine_half_t* W_gu,
+                                                          engine_half_t* Y, int64_t M, int64_t F,
+                                                          int64_t K, float eps,
+                                                          engine_stream_t stream);
+
 /* out[i] = silu(gate[i]) * up[i], FP16: glue between the gate/up and down
  * projections of the tensor-parallel layer.  kernels.hpp:141 (swiglu_fp16). */
 ENGINE_B200_API int engine_cuda_swiglu_f16(const engine_half_t* gate, const engine_half_t* up,

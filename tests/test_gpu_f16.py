@@ -310,6 +310,46 @@ def test_rmsnorm_linear_f16_residual(pkg, dev, M):
     bounds.check(host(Y).astype(np.float32), exact, bound, f"resid M={M}")
 
 
+@pytest.mark.parametrize("M,F,gamma", [(1, 1792, True), (1, 14336, True), (1, 3584, False),
+                                       (3, 1792, True), (16, 3584, True)])
+def test_rmsnorm_linear_swiglu_fused(pkg, dev, M, F, gamma):
+    """The fused gate/up projection + SwiGLU equals rmsnorm_linear_f16 into
+    [M, 2F] followed by swiglu_f16, bit for bit (batch 1: one kernel; larger
+    batches: scratch + the same two steps), and the oracle composition of the
+    reference's ops within a derived bound."""
+    K = 4096
+    rng = np.random.default_rng(M * 1000 + F)
+    x = f16(rng, (M, K))
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16)
+    W = f16(rng, (2 * F, K), 0.02)
+    tx, tg, tw = dev_t(x), dev_t(g), dev_t(W)
+    gp = tg if gamma else None
+    fused = pkg.ops.rmsnorm_linear_swiglu(tx, gp, tw, EPS)
+    gu = pkg.ops.rmsnorm_linear(tx, gp, tw, EPS)
+    ref = pkg.ops.swiglu(gu[:, :F].contiguous(), gu[:, F:].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(fused, ref)
+    # Oracle composition: gate/up rounded to FP16, then silu(g) * u.  The GPU's and
+    # the oracle's g (and u) are each within the derived GEMV bound of the exact
+    # projection, so |dg| <= 2 * gemv16_bound; with |silu'| <= 1.1,
+    # |d(silu(g) u)| <= 1.1 |dg| |u| + |silu(g)| |du| + 1.1 |dg| |du|, plus the
+    # final FP16 rounding of each side.
+    gm = g if gamma else None
+    go, exact = oracle.rmsnorm_linear_f16(x, gm, W, EPS, want_f32=True, nthreads=8)
+    want = oracle.swiglu_f16(np.ascontiguousarray(go[:, :F]), np.ascontiguousarray(go[:, F:]))
+    tn = oracle.rmsnorm(x.astype(np.float32), g.astype(np.float32) if gamma else None, EPS)
+    absdot = np.abs(tn.astype(np.float64)) @ np.abs(W.astype(np.float64)).T
+    d = 2 * bounds.gemv16_bound(K, absdot, exact)
+    dg, du = d[:, :F], d[:, F:]
+    gv = go[:, :F].astype(np.float64)
+    uv = np.abs(go[:, F:].astype(np.float64))
+    silu = np.abs(gv / (1 + np.exp(-gv)))
+    w64 = want.astype(np.float64)
+    bound = 1.1 * dg * uv + silu * du + 1.1 * dg * du + 2 * bounds.U16 * np.abs(w64) + 2.0 ** -24
+    bounds.check(host(fused).astype(np.float64), w64, bound,
+                 f"fused swiglu M={M} F={F}")
+
+
 def test_swiglu_and_embedding_glue(pkg, dev):
     rng = np.random.default_rng(0)
     n = 14336 * 2 + 3

@@ -34,6 +34,12 @@ class CpuOps:
         g = g.double()
         return g / (1 + torch.exp(-g)) * u.double()
 
+    def rmsnorm_linear_swiglu(self, x, gamma, W_gu, eps, out=None):
+        self.calls.append("rmsnorm_linear_swiglu")
+        gu = self.rmsnorm_linear(x, gamma, W_gu, eps)
+        f = W_gu.shape[0] // 2
+        return self.swiglu(gu[:, :f], gu[:, f:])
+
     def embedding(self, table, ids, out=None):
         self.calls.append("embedding")
         return table[ids.long()].double()
