@@ -3,7 +3,9 @@
 //
 // One process per GPU.  Each rank allocates one device region:
 //
-//   recv   [2 parities][world sources][cap]  u64  {FP32 bits, call number} words
+//   recv   [2 parities][world sources][cap]  u64  {payload, call number} words:
+//          the payload is one FP32 partial (fused projection) or two FP16
+//          partials (all-reduce of an FP16 tensor)
 //   epoch  [kTpCtas]                         u32  this rank's call count, per CTA
 //
 // The ranks exchange the regions' CUDA IPC handles through the host (the
@@ -92,10 +94,10 @@ __device__ __forceinline__ unsigned long long* tp_slot(const TpArgs& a, int dst,
   return a.recv[dst] + (static_cast<int64_t>(e & 1u) * a.world + src) * a.cap;
 }
 
-/// Stores value v of element idx, tagged with call e, into every rank's slot.
-__device__ __forceinline__ void tp_push(const TpArgs& a, uint32_t e, int64_t idx, float v) {
-  const unsigned long long w =
-      (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+/// Stores 32 payload bits for word idx, tagged with call e, into every rank's slot.
+__device__ __forceinline__ void tp_push_bits(const TpArgs& a, uint32_t e, int64_t idx,
+                                             uint32_t bits) {
+  const unsigned long long w = (static_cast<unsigned long long>(e) << 32) | bits;
 #pragma unroll
   for (int s = 0; s < kTpMaxWorld; ++s) {  // static indices keep the pointers in registers
     if (s < a.world) {
@@ -106,30 +108,62 @@ __device__ __forceinline__ void tp_push(const TpArgs& a, uint32_t e, int64_t idx
   }
 }
 
+/// Stores FP32 value v of element idx, tagged with call e, into every rank's slot.
+__device__ __forceinline__ void tp_push(const TpArgs& a, uint32_t e, int64_t idx, float v) {
+  tp_push_bits(a, e, idx, __float_as_uint(v));
+}
+
+/// Reads word idx of call e from source s's slot (re-reading until its tag is
+/// e; bounded by the wait limit).  Returns false on a time-out.
+__device__ __forceinline__ bool tp_wait_word(const TpArgs& a, const unsigned long long* p,
+                                             uint32_t e, uint32_t& bits,
+                                             unsigned long long& t0) {
+  unsigned long long w;
+  int spins = 0;
+  while (true) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if (static_cast<uint32_t>(w >> 32) == e) break;
+    if ((++spins & 63) == 0) {
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) t0 = now;
+      if (now - t0 > a.limit_ns) {
+        if (a.err) atomicOr(a.err, kErrWaitTimeout);
+        return false;
+      }
+    }
+  }
+  bits = static_cast<uint32_t>(w);
+  return true;
+}
+
+/// Sums over sources 0..world-1 (in that order) of the half2 word idx of call e.
+__device__ __forceinline__ bool tp_gather_h2(const TpArgs& a, uint32_t e, int64_t idx, float& v0,
+                                             float& v1, unsigned long long& t0) {
+  const unsigned long long* base = a.own + static_cast<int64_t>(e & 1u) * a.world * a.cap + idx;
+  float s0 = 0.0f, s1 = 0.0f;
+  for (int s = 0; s < a.world; ++s) {
+    uint32_t bits;
+    if (!tp_wait_word(a, base + s * a.cap, e, bits, t0)) return false;
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&bits));
+    s0 += f.x;
+    s1 += f.y;
+  }
+  v0 = s0;
+  v1 = s1;
+  return true;
+}
+
 /// Sum over sources 0..world-1 (in that order) of element idx of call e.  Each
 /// word is re-read until its tag is e; gives up after the wait limit (sets the
 /// device error word, returns false).
 __device__ __forceinline__ bool tp_gather(const TpArgs& a, uint32_t e, int64_t idx, float& sum,
                                           unsigned long long& t0) {
-  float v = 0.0f;
   const unsigned long long* base = a.own + static_cast<int64_t>(e & 1u) * a.world * a.cap + idx;
+  float v = 0.0f;
   for (int s = 0; s < a.world; ++s) {
-    const unsigned long long* p = base + s * a.cap;
-    unsigned long long w;
-    int spins = 0;
-    while (true) {
-      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-      if (static_cast<uint32_t>(w >> 32) == e) break;
-      if ((++spins & 63) == 0) {
-        const unsigned long long now = globaltimer();
-        if (t0 == 0) t0 = now;
-        if (now - t0 > a.limit_ns) {
-          if (a.err) atomicOr(a.err, kErrWaitTimeout);
-          return false;
-        }
-      }
-    }
-    v += __uint_as_float(static_cast<uint32_t>(w));
+    uint32_t bits;
+    if (!tp_wait_word(a, base + s * a.cap, e, bits, t0)) return false;
+    v += __uint_as_float(bits);
   }
   sum = v;
   return true;
@@ -186,8 +220,10 @@ __global__ void __launch_bounds__(kNkVecWarps * 32, 2)
   }
 }
 
-// All-reduce of an FP16 partial P[n] (any producer): Y = sum_s P_s + R.  CTA b
-// owns elements [b*per, (b+1)*per).
+// All-reduce of an FP16 partial P[n] (any producer): Y = sum_s P_s + R.  The
+// values already are FP16, so each tagged word carries TWO of them (a half2 in
+// the low half): half the NVLink bytes of FP32 words, the same sums.  CTA b
+// owns element pairs [b*per, (b+1)*per).
 __global__ void __launch_bounds__(256, 2)
     tp_allreduce_kernel(const TpArgs a, const __half* __restrict__ P,
                         const __half* __restrict__ R, __half* __restrict__ Y, int64_t n,
@@ -196,15 +232,25 @@ __global__ void __launch_bounds__(256, 2)
   pdl_trigger();
   pdl_wait();
   const uint32_t e = tp_begin(a, &s_e);
+  const int64_t npairs = (n + 1) / 2;
   const int64_t lo = static_cast<int64_t>(blockIdx.x) * per;
-  const int64_t hi = (lo + per < n) ? lo + per : n;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) tp_push(a, e, i, __half2float(P[i]));
+  const int64_t hi = (lo + per < npairs) ? lo + per : npairs;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const __half x0 = P[2 * i];
+    const __half x1 = (2 * i + 1 < n) ? P[2 * i + 1] : __float2half_rn(0.0f);
+    const __half2 h = __halves2half2(x0, x1);
+    tp_push_bits(a, e, i, *reinterpret_cast<const uint32_t*>(&h));
+  }
   unsigned long long t0 = 0;
   for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    float v;
-    if (!tp_gather(a, e, i, v, t0)) return;
-    if (R != nullptr) v += __half2float(R[i]);
-    Y[i] = __float2half_rn(v);
+    float v0 = 0.0f, v1 = 0.0f;
+    if (!tp_gather_h2(a, e, i, v0, v1, t0)) return;
+    if (R != nullptr) v0 += __half2float(R[2 * i]);
+    Y[2 * i] = __float2half_rn(v0);
+    if (2 * i + 1 < n) {
+      if (R != nullptr) v1 += __half2float(R[2 * i + 1]);
+      Y[2 * i + 1] = __float2half_rn(v1);
+    }
   }
 }
 
@@ -244,7 +290,7 @@ int check_comm(const engine_tp_comm* c) {
 
 int launch_allreduce(const engine_tp_comm* c, const __half* P, const __half* R, __half* Y,
                      int64_t n, cudaStream_t stream) {
-  const int64_t per = (n + kTpCtas - 1) / kTpCtas;
+  const int64_t per = ((n + 1) / 2 + kTpCtas - 1) / kTpCtas;  // element pairs per CTA
   B200_CUDA(launch_pdl(tp_allreduce_kernel, dim3(kTpCtas), dim3(256), 0, stream, make_args(c), P,
                        R, Y, n, per));
   return check_launch("tp_allreduce_f16");
