@@ -220,6 +220,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+/// Prefetches one tensor-map tile into L2 (no shared memory, no barrier).  L2 is
+/// the device's point of coherence: issued before griddepcontrol.wait it can
+/// never hand stale data to a later load.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map,
                                                  uint64_t* bar, int32_t x, int32_t y,
                                                  uint64_t policy) {

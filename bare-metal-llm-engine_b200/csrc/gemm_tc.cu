@@ -431,11 +431,6 @@ __global__ void __launch_bounds__(kThreads)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) TC_TRACE(1);
-  // Set-up done: let the next kernel start launching, then wait for the previous
-  // one (no operand or output is touched before this point).
-  pdl_trigger();
-  pdl_wait();
-
   const int64_t num_tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   const int z = static_cast<int>(blockIdx.z);
   const int64_t kb0 = static_cast<int64_t>(z) * p.kb_per_split;
@@ -443,6 +438,23 @@ __global__ void __launch_bounds__(kThreads)
   const bool have_k = kb1 > kb0;
   const int64_t t_begin = blockIdx.x;
   const int64_t t_step = (p.split > 1) ? num_tiles : gridDim.x;  // split: one tile per CTA
+  // Set-up done: let the next kernel start launching, then wait for the previous
+  // one (no operand or output is read or written before the wait).
+  pdl_trigger();
+  if constexpr (SWAP) {
+    // The weight tiles (operand A here) never depend on the preceding kernel --
+    // typically the small activation pre-pass, which leaves most SMs free:
+    // pull this CTA's first ST weight tiles into L2 meanwhile.  L2 is coherent,
+    // so this cannot return stale data; the TMA loads after the wait hit L2.
+    if (warp == 0 && lane == 0 && have_k && t_begin < num_tiles) {
+      int tm, tn;
+      tile_coords(t_begin, p.tiles_m, p.tiles_n, tm, tn);
+      const int64_t kend = (kb1 < kb0 + ST) ? kb1 : kb0 + ST;
+      for (int64_t kb = kb0; kb < kend; ++kb)
+        tma_prefetch_2d(&tmA, static_cast<int32_t>(kb * kBK), tm * kBM);
+    }
+  }
+  pdl_wait();
 
   constexpr uint32_t kIdesc = umma_idesc_f16(kBM, BN, BF16, false, B_MN);
 

@@ -21,8 +21,11 @@
 namespace b200 {
 namespace {
 
-// One block per activation row.  Output rows [0, M) = hi, [hb, hb + M) = lo;
-// the padding rows [M, hb) and [hb + M, 2 hb) are written as zeros.
+// Block (r, s) of a (hb x P) grid: activation row r, K slice s of P.  Output
+// rows [0, M) = hi, [hb, hb + M) = lo; the padding rows [M, hb) and
+// [hb + M, 2 hb) are written as zeros.  Every block of a row forms the row's
+// scale from the whole row (the same threads and order, so the same scale); it
+// then converts only its slice, 8 elements per 16-byte access.
 __global__ void __launch_bounds__(256) rmsnorm_hilo_kernel(const __half* __restrict__ x,
                                                            const __half* __restrict__ gamma,
                                                            __half* __restrict__ out, int64_t M,
@@ -32,18 +35,33 @@ __global__ void __launch_bounds__(256) rmsnorm_hilo_kernel(const __half* __restr
   pdl_trigger();
   pdl_wait();
   const int64_t r = blockIdx.x;  // 0 .. hb-1
+  const int64_t P = gridDim.y;
+  const int64_t s = blockIdx.y;
   __half* hi = out + r * K;
   __half* lo = out + (r + hb) * K;
+  const bool vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                   (gamma == nullptr || reinterpret_cast<uintptr_t>(gamma) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  // This block's slice, in 8-element chunks when vectorised.
+  const int64_t units = vec ? K / 8 : K;
+  const int64_t u0 = units * s / P;
+  const int64_t u1 = units * (s + 1) / P;
   if (r >= M) {
-    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-      hi[k] = __float2half_rn(0.0f);
-      lo[k] = __float2half_rn(0.0f);
+    if (vec) {
+      for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+        reinterpret_cast<uint4*>(hi)[u] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(lo)[u] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      for (int64_t k = u0 + threadIdx.x; k < u1; k += blockDim.x) {
+        hi[k] = __float2half_rn(0.0f);
+        lo[k] = __float2half_rn(0.0f);
+      }
     }
     return;
   }
   const __half* src = x + r * K;
   double ss = 0.0;
-  const bool vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0);
   if (vec) {  // 16-byte loads: one pass over the row in a few iterations
     for (int64_t k8 = threadIdx.x; k8 < K / 8; k8 += blockDim.x) {
       const uint4 raw = *reinterpret_cast<const uint4*>(src + 8 * k8);
@@ -72,12 +90,31 @@ __global__ void __launch_bounds__(256) rmsnorm_hilo_kernel(const __half* __restr
   }
   __syncthreads();
   const float scale = s_scale;
-  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-    const float g = gamma ? __half2float(gamma[k]) : 1.0f;
-    const float t = __fmul_rn(__fmul_rn(__half2float(src[k]), scale), g);
-    const __half h = __float2half_rn(t);
-    hi[k] = h;
-    lo[k] = __float2half_rn(__fsub_rn(t, __half2float(h)));
+  auto split = [&](float xv, float g, __half& h, __half& l) {
+    const float t = __fmul_rn(__fmul_rn(xv, scale), g);
+    h = __float2half_rn(t);
+    l = __float2half_rn(__fsub_rn(t, __half2float(h)));
+  };
+  if (vec) {
+    for (int64_t u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+      const uint4 xr = reinterpret_cast<const uint4*>(src)[u];
+      const uint4 gr = gamma ? reinterpret_cast<const uint4*>(gamma)[u]
+                             : make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+      const __half* xh = reinterpret_cast<const __half*>(&xr);
+      const __half* gh = reinterpret_cast<const __half*>(&gr);
+      uint4 ho, lo4;
+      __half* hp = reinterpret_cast<__half*>(&ho);
+      __half* lp = reinterpret_cast<__half*>(&lo4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split(__half2float(xh[i]), __half2float(gh[i]), hp[i], lp[i]);
+      reinterpret_cast<uint4*>(hi)[u] = ho;
+      reinterpret_cast<uint4*>(lo)[u] = lo4;
+    }
+  } else {
+    for (int64_t k = u0 + threadIdx.x; k < u1; k += blockDim.x) {
+      const float g = gamma ? __half2float(gamma[k]) : 1.0f;
+      split(__half2float(src[k]), g, hi[k], lo[k]);
+    }
   }
 }
 
@@ -109,7 +146,10 @@ int linear_impl(const void* X, const void* W, const void* R, void* Y, int64_t M,
 
 int rmsnorm_hilo(const __half* x, const __half* gamma, __half* out, int64_t M, int64_t K, int hb,
                  float eps, cudaStream_t stream) {
-  B200_CUDA(launch_pdl(rmsnorm_hilo_kernel, dim3(hb), dim3(256), 0, stream, x, gamma, out, M, K,
+  // Slices of >= 2048 elements per block, at most 8 per row.
+  const unsigned P = static_cast<unsigned>(K >= 16384 ? 8 : (K + 2047) / 2048);
+  B200_CUDA(launch_pdl(rmsnorm_hilo_kernel, dim3(hb, P > 0 ? P : 1), dim3(256), 0, stream, x,
+                       gamma, out, M, K,
                        hb, eps));
   return check_launch("rmsnorm_linear_f16 (normalise)");
 }
