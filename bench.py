@@ -23,6 +23,8 @@ reference has no GPU path for this configuration) and prints its line.
 projection layer set instead (see bare-metal-llm-engine_b200/tp.py);
 ``--workload tp-comm`` (torchrun, >= 2 GPUs) times the row-split projection with
 its all-reduce: NVLink fused vs NVLink / NCCL after the projection.
+``--workload kernel --case NAME`` runs one configuration alone for a few
+launches (the ncu summaries in profiles/ are captured on it).
 """
 from __future__ import annotations
 
@@ -532,14 +534,71 @@ def run_headline(args):
     return 0
 
 
+KERNEL_CASES = ("gemm4096", "gemv_4096x14336", "rmsnorm_qkv_b1", "rmsnorm_qkv_b16",
+                "matmul_f32_512", "prefill_s2048")
+
+
+def run_kernel_case(args) -> int:
+    """--workload kernel --case NAME: one BASELINE configuration alone, `warmup`
+    then `steps` launches on the current stream (no graphs), for profiling a
+    single kernel with few launches before it.  Prints the mean per-launch time."""
+    import torch
+
+    pkg = load_pkg()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(20260826)
+    st = torch.cuda.current_stream().cuda_stream
+    c = args.case
+    if c == "gemm4096":
+        n = 4096
+        sets = [tuple(torch.randn(n, n, device=dev, generator=g).half() for _ in range(2)) +
+                (torch.empty(n, n, device=dev, dtype=torch.float16),) for _ in range(2)]
+        fn = lambda s: pkg.cuda.matmul_f16(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)  # noqa: E731
+    elif c == "gemv_4096x14336":
+        N, K = 4096, 14336
+        sets = [((torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.gemv_f16_nk(s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), N, K, st)  # noqa: E731
+    elif c in ("rmsnorm_qkv_b1", "rmsnorm_qkv_b16"):
+        N, K = 6144, 4096
+        B = 1 if c.endswith("b1") else 16
+        sets = [(torch.randn(B, K, device=dev, generator=g).half(),
+                 (1 + 0.1 * torch.randn(K, device=dev, generator=g)).half(),
+                 (torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.empty(B, N, device=dev, dtype=torch.float16)) for _ in range(3)]
+        fn = lambda s: pkg.cuda.rmsnorm_linear_f16(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0,  # noqa: E731
+                                                   s[3].data_ptr(), B, N, K, 1e-5, st)
+    elif c == "matmul_f32_512":
+        n = 512
+        sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.empty(n, n, device=dev)) for _ in range(48)]
+        fn = lambda s: pkg.cuda.matmul_register_tiled(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)  # noqa: E731
+    else:  # prefill_s2048
+        S, N, K = 2048, 14336, 4096
+        sets = [(torch.randn(S, K, device=dev, generator=g).half(),
+                 (torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.empty(S, N, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.linear_f16(s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), S, N, K, st)  # noqa: E731
+    stream = torch.cuda.current_stream()
+    per, total = time_launches(torch, fn, sets, args.steps, args.warmup, stream)
+    print(json.dumps({"workload": "kernel", "case": c, "steps": args.steps, "warmup": args.warmup,
+                      "us_per_launch": 1e3 * statistics.mean(per),
+                      "timing": "CUDA events per launch, rotating operand sets"}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["headline", "tp-decode", "tp-prefill", "tp-comm"],
+    ap.add_argument("--workload", choices=["headline", "tp-decode", "tp-prefill", "tp-comm", "kernel"],
                     default="headline")
+    ap.add_argument("--case", choices=KERNEL_CASES, default="gemm4096",
+                    help="--workload kernel: the configuration to run alone")
     ap.add_argument("--batch", type=int, default=1, help="tp-decode batch (1 or 32)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
@@ -549,6 +608,8 @@ def main() -> int:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "kernel":
+        return run_kernel_case(args)
     if args.workload != "headline":
         tp = importlib.import_module("bmle_b200.tp") if "bmle_b200" in sys.modules else None
         load_pkg()
