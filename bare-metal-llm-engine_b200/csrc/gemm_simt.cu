@@ -24,6 +24,8 @@
 //     normalised activation never touches global memory.
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -212,9 +214,18 @@ int launch_sgemm(const float* A, const float* B, float* C, int64_t M, int64_t N,
   B200_REQUIRE(gx <= 0x7fffffff, "matmul: N too large");
   const int sms = sm_count();
   const int64_t tiles = gx * gy;
+  // Split K over a cluster of S CTAs while the tiles alone cannot fill `waves`
+  // CTAs per SM.  The kernel is small (48 registers, 16 KB static shared
+  // memory), so four fit per SM; on B200 waves = 4 took 512^3 from 27.7 to
+  // 19.0 us per launch (S = 8, 512 CTAs).  ENGINE_SGEMM_WAVES overrides.
+  static const int waves_env = [] {
+    const char* e = std::getenv("ENGINE_SGEMM_WAVES");
+    return (e && e[0]) ? static_cast<int>(std::strtol(e, nullptr, 10)) : 4;
+  }();
+  const int64_t slots = static_cast<int64_t>(sms) * (waves_env > 0 ? waves_env : 1);
   int S = 1;
-  if (tiles < sms) {
-    S = static_cast<int>(sms / tiles);
+  if (tiles < slots) {
+    S = static_cast<int>(slots / tiles);
     if (S > 8) S = 8;
     const int64_t kmax = (K + 63) / 64;  // keep at least 64 of K per split
     if (S > kmax) S = static_cast<int>(kmax);

@@ -174,3 +174,18 @@ def test_tp_comm_rejects_bad_arguments(pkg):
     with pytest.raises(pkg.EngineError):
         c.tp_comm_handle(0)
     c.tp_comm_destroy(0)  # destroying nothing is a no-op
+
+
+def test_fused_swiglu_entry_rejects_bad_arguments(pkg):
+    """engine_cuda_rmsnorm_linear_swiglu_f16 follows the rmsnorm_linear contract."""
+    c = pkg.cuda
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, P, P, -1, 4, 4, 1e-5, substr="negative")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, P, P, 1, -4, 4, 1e-5, substr="negative")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, P, P, 1, 4, -4, 1e-5, substr="negative")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, 0, P, P, P, 1, 4, 4, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, 0, P, 1, 4, 4, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, P, 0, 1, 4, 4, 1e-5, substr="null")
+    _throws(pkg, c.rmsnorm_linear_swiglu_f16, P, P, P, P, 1, 4, 4, -1e-5, substr="eps")
+    # empty work is a no-op (nothing is launched), gamma may be null
+    c.rmsnorm_linear_swiglu_f16(P, 0, P, P, 0, 4, 4, 1e-5)
+    c.rmsnorm_linear_swiglu_f16(P, 0, P, P, 2, 0, 4, 1e-5)
