@@ -19,7 +19,7 @@ dependency), records:
 Outputs: ``hotpath_cases.json`` and ``hotpath_expected.npz`` beside this file.
 Run it only where the reference tree exists (it is not needed on the GPU box):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference source tree>]
 """
 from __future__ import annotations
 
