@@ -15,6 +15,7 @@
 // otherwise a compatible engine::EngineError is declared here.
 //===----------------------------------------------------------------------===//
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -43,6 +44,10 @@ inline void check(int rc) {
 }
 inline const engine_half_t* h(const __half* p) { return reinterpret_cast<const engine_half_t*>(p); }
 inline engine_half_t* h(__half* p) { return reinterpret_cast<engine_half_t*>(p); }
+inline const engine_bf16_t* b(const __nv_bfloat16* p) {
+  return reinterpret_cast<const engine_bf16_t*>(p);
+}
+inline engine_bf16_t* b(__nv_bfloat16* p) { return reinterpret_cast<engine_bf16_t*>(p); }
 }  // namespace b200_detail
 
 // -- kernels.hpp:62-104, 120: the legacy hot-path launchers ------------------
@@ -131,5 +136,78 @@ inline void rmsnorm_linear_f16(const __half* x, const __half* gamma, const __hal
       b200_detail::h(x), b200_detail::h(gamma), b200_detail::h(W), b200_detail::h(residual),
       b200_detail::h(Y), M, N, K, eps, stream));
 }
+
+inline void matmul_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C,
+                        std::int64_t M, std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_matmul_bf16(b200_detail::b(A), b200_detail::b(B),
+                                             b200_detail::b(C), M, N, K, stream));
+}
+
+inline void linear_bf16(const __nv_bfloat16* X, const __nv_bfloat16* W,
+                        const __nv_bfloat16* residual, __nv_bfloat16* Y, std::int64_t M,
+                        std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_linear_bf16(b200_detail::b(X), b200_detail::b(W),
+                                             b200_detail::b(residual), b200_detail::b(Y), M, N,
+                                             K, stream));
+}
+
+// Fused RMSNorm -> gate/up projection -> SwiGLU: rmsnorm_linear followed by
+// swiglu_fp16 in one call (W_gu = gate rows, then up rows).
+inline void rmsnorm_linear_swiglu_fp16(const __half* x, const __half* gamma, const __half* W_gu,
+                                       __half* Y, std::int64_t M, std::int64_t F, std::int64_t K,
+                                       float eps, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_rmsnorm_linear_swiglu_f16(
+      b200_detail::h(x), b200_detail::h(gamma), b200_detail::h(W_gu), b200_detail::h(Y), M, F, K,
+      eps, stream));
+}
+
+// kernels.hpp:128 (embedding_fp16)
+inline void embedding_fp16(const __half* table, const std::int32_t* ids, __half* out,
+                           std::int64_t num_tokens, std::int64_t hidden, std::int64_t vocab,
+                           cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_embedding_f16(b200_detail::h(table), ids, b200_detail::h(out),
+                                               num_tokens, hidden, vocab, stream));
+}
+
+// -- tensor-parallel communicator (engine_tp_*) --------------------------------
+// One per rank, on the rank's current device.  The host exchanges handle()
+// between the ranks (all-gather), then calls open() with all of them in rank
+// order.  Destroy only after a host barrier across the ranks.
+class TpComm {
+ public:
+  TpComm(int rank, int world, std::int64_t max_elems) {
+    b200_detail::check(engine_tp_comm_create(rank, world, max_elems, &comm_));
+  }
+  ~TpComm() { engine_tp_comm_destroy(comm_); }
+  TpComm(const TpComm&) = delete;
+  TpComm& operator=(const TpComm&) = delete;
+
+  std::string handle() const {
+    std::string h(ENGINE_TP_HANDLE_BYTES, '\0');
+    b200_detail::check(engine_tp_comm_handle(comm_, &h[0]));
+    return h;
+  }
+  void open(const std::string& all_handles) {
+    b200_detail::check(engine_tp_comm_open(comm_, all_handles.data()));
+  }
+  // y = sum over ranks of partial (+ residual), on every rank
+  void allreduce(const __half* partial, const __half* residual, __half* y, std::int64_t n,
+                 cudaStream_t stream = 0) {
+    b200_detail::check(engine_tp_allreduce_f16(comm_, b200_detail::h(partial),
+                                               b200_detail::h(residual), b200_detail::h(y), n,
+                                               stream));
+  }
+  // Y = sum over ranks of X_r W_r^T (+ residual): the row-split projection fused
+  // with its all-reduce
+  void linear_allreduce(const __half* X, const __half* W, const __half* residual, __half* Y,
+                        std::int64_t M, std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+    b200_detail::check(engine_tp_linear_allreduce_f16(
+        comm_, b200_detail::h(X), b200_detail::h(W), b200_detail::h(residual), b200_detail::h(Y),
+        M, N, K, stream));
+  }
+
+ private:
+  engine_tp_comm_t* comm_ = nullptr;
+};
 
 }  // namespace engine::cuda
