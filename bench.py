@@ -535,7 +535,7 @@ def run_headline(args):
 
 
 KERNEL_CASES = ("gemm4096", "gemv_4096x14336", "rmsnorm_qkv_b1", "rmsnorm_qkv_b16",
-                "matmul_f32_512", "prefill_s2048")
+                "matmul_f32_512", "prefill_s2048", "gate_up_swiglu_b1", "tp_down_b1_world1")
 
 
 def run_kernel_case(args) -> int:
@@ -575,6 +575,24 @@ def run_kernel_case(args) -> int:
                  torch.rand(n, n, device=dev, generator=g) * 2 - 1,
                  torch.empty(n, n, device=dev)) for _ in range(48)]
         fn = lambda s: pkg.cuda.matmul_register_tiled(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)  # noqa: E731
+    elif c == "gate_up_swiglu_b1":  # Llama-3-8B gate/up (2 x 14336 rows) + SwiGLU, batch 1
+        F, K = 14336, 4096
+        sets = [(torch.randn(1, K, device=dev, generator=g).half(),
+                 (1 + 0.1 * torch.randn(K, device=dev, generator=g)).half(),
+                 (torch.randn(2 * F, K, device=dev, generator=g) * 0.02).half(),
+                 torch.empty(1, F, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.rmsnorm_linear_swiglu_f16(s[0].data_ptr(), s[1].data_ptr(),  # noqa: E731
+                                                          s[2].data_ptr(), s[3].data_ptr(), 1, F, K,
+                                                          1e-5, st)
+    elif c == "tp_down_b1_world1":  # the fused row-split down projection + all-reduce, one rank
+        N, K = 4096, 14336
+        comm = pkg.tp.NvlinkComm(0, 1, N)
+        sets = [(torch.randn(1, K, device=dev, generator=g).half(),
+                 (torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(1, N, device=dev, generator=g).half(),
+                 torch.empty(1, N, device=dev, dtype=torch.float16)) for _ in range(4)]
+        fn = lambda s: pkg.cuda.tp_linear_allreduce_f16(comm.handle, s[0].data_ptr(), s[1].data_ptr(),  # noqa: E731
+                                                        s[2].data_ptr(), s[3].data_ptr(), 1, N, K, st)
     else:  # prefill_s2048
         S, N, K = 2048, 14336, 4096
         sets = [(torch.randn(S, K, device=dev, generator=g).half(),
