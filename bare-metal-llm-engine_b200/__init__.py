@@ -59,6 +59,8 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_swiglu_f16": [_p, _p, _p, _i64, _p],
     "engine_cuda_rmsnorm_linear_swiglu_f16": [_p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_embedding_f16": [_p, _p, _p, _i64, _i64, _i64, _p],
+    "engine_cuda_quant_repack": [ctypes.c_int, _p, _p, _p, _i64, _i64, _p],
+    "engine_cuda_gemv_q_nk": [ctypes.c_int, _p, _p, _p, _p, _p, _i64, _i64, _p],
     "engine_tp_comm_create": [ctypes.c_int, ctypes.c_int, _i64, ctypes.POINTER(ctypes.c_void_p)],
     "engine_tp_comm_handle": [_p, _p],
     "engine_tp_comm_open": [_p, _p],

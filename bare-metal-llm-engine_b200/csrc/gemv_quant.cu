@@ -1,0 +1,254 @@
+// gemv_quant.cu -- decode GEMV over block-quantised weights (Q8_0 / Q4_0).
+//
+// Format (GGUF's, as declared by the engine: include/engine/dtype.hpp:95-125,
+// kQuantBlockSize = 32).  A row of K weights is K/32 blocks, each with one FP16
+// scale d:
+//   Q8_0 block: { half d; int8  q[32]; }        34 bytes, w[i] = d * q[i]
+//   Q4_0 block: { half d; uint8 nib[16]; }      18 bytes, w[j] = d * (lo(nib[j]) - 8),
+//                                                         w[j+16] = d * (hi(nib[j]) - 8)
+// GGUF stores these blocks packed back to back (34- and 18-byte strides), which
+// is not 16-byte aligned.  engine_cuda_quant_repack() converts them once, at load
+// time, into the layout the GEMV streams:
+//   payload  [N][K] int8 (Q8_0) or [N][K/2] nibble bytes (Q4_0, each block's 16
+//            bytes kept in the GGUF order), 16-byte aligned rows;
+//   scales   [N][K/32] FP16.
+//
+// GEMV: y[n] = sum_b d[n,b] * (sum_{i<32} q[n,32b+i] * x[32b+i]) (+ residual).
+// - Each lane owns whole blocks; the 32 lanes of a warp cover 32 consecutive
+//   blocks of a row: 1 KB of Q8_0 or 512 B of Q4_0 payload per warp step.
+// - Payload loads are 16-byte `ld.global.nc.L1::no_allocate`; scales (64 B per
+//   warp step) and x come through L1.
+// - The 32 products of a block are exact in FP32 (a 19-bit integer times a
+//   half); they are summed in FP32, multiplied by d and accumulated per lane.
+// - The warp shuffle and the cross-warp sum run in fixed order.
+// HBM bytes per weight: 1.0625 (Q8_0) or 0.5625 (Q4_0), against 2 for FP16.
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "kernels.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kQWarps = 8;
+
+// One GGUF block -> the split layout.  One thread per block.
+template <int QT>
+__global__ void quant_repack_kernel(const uint8_t* __restrict__ blocks, uint8_t* __restrict__ q,
+                                    __half* __restrict__ d, int64_t N, int64_t nblk) {
+  constexpr int PAY = QT == 8 ? 32 : 16;
+  constexpr int BLK = 2 + PAY;
+  pdl_trigger();
+  pdl_wait();
+  const int64_t total = N * nblk;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* src = blocks + i * BLK;
+    const uint16_t bits = static_cast<uint16_t>(src[0] | (src[1] << 8));
+    d[i] = __ushort_as_half(bits);
+    uint8_t* dst = q + i * PAY;  // row n, block b: (n * nblk + b) * PAY
+#pragma unroll
+    for (int k = 0; k < PAY; ++k) dst[k] = src[2 + k];
+  }
+}
+
+/// sum_i q_i * x_i over one block; xv = the block's 32 x values (4 x uint4).
+template <int QT>
+__device__ __forceinline__ float block_dot(const uint4 (&p)[2], const uint4 (&xv)[4]) {
+  float xf[32];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float t[8];
+    h8_to_f8(xv[c], t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xf[8 * c + i] = t[i];
+  }
+  float s = 0.0f;
+  if constexpr (QT == 8) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&p[0]);  // 8 words = 32 int8
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int v = static_cast<int8_t>((w[i >> 2] >> (8 * (i & 3))) & 0xffu);
+      s = fmaf(static_cast<float>(v), xf[i], s);
+    }
+  } else {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&p[0]);  // 4 words = 16 bytes
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
+      s = fmaf(static_cast<float>(static_cast<int>(byte & 0xfu) - 8), xf[j], s);
+      s = fmaf(static_cast<float>(static_cast<int>(byte >> 4) - 8), xf[j + 16], s);
+    }
+  }
+  return s;
+}
+
+template <int QT, int RPW, int SK, bool RESID>
+__global__ void __launch_bounds__(kQWarps * 32) gemv_q_kernel(
+    const uint8_t* __restrict__ q, const __half* __restrict__ d, const __half* __restrict__ x,
+    const __half* __restrict__ R, __half* __restrict__ y, int64_t N, int64_t K) {
+  constexpr int GROUPS = kQWarps / SK;
+  constexpr int PAY = QT == 8 ? 32 : 16;  // payload bytes per block
+  __shared__ float red[kQWarps][RPW];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int grp = warp / SK;
+  const int sub = warp % SK;
+  const int64_t nblk = K / 32;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * GROUPS + grp) * RPW;
+  const uint8_t* prow[RPW];
+  const __half* drow[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int64_t n = (row0 + r < N) ? row0 + r : N - 1;  // clamped rows: not stored
+    prow[r] = q + n * nblk * PAY;
+    drow[r] = d + n * nblk;
+  }
+  const int64_t b0 = static_cast<int64_t>(sub) * 32 + lane;
+  constexpr int64_t kStride = 32 * SK;
+  pdl_trigger();
+  if (row0 < N && b0 < nblk) {  // warm L2 with this lane's first payload block
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) prefetch_l2(prow[r] + b0 * PAY);
+  }
+  pdl_wait();
+
+  float acc[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+  if (row0 < N) {
+#pragma unroll 2
+    for (int64_t b = b0; b < nblk; b += kStride) {
+      uint4 p[RPW][2];
+      float sc[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        p[r][0] = ld_stream_v4(prow[r] + b * PAY);
+        p[r][1] = (QT == 8) ? ld_stream_v4(prow[r] + b * PAY + 16) : make_uint4(0, 0, 0, 0);
+        sc[r] = __half2float(drow[r][b]);
+      }
+      uint4 xv[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xv[c] = __ldg(reinterpret_cast<const uint4*>(x + 32 * b) + c);
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) acc[r] = fmaf(sc[r], block_dot<QT>(p[r], xv), acc[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) red[warp][r] = acc[r];
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < GROUPS * RPW; o += blockDim.x) {
+    const int g = o / RPW;
+    const int r = o % RPW;
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * GROUPS + g) * RPW + r;
+    if (row >= N) continue;
+    float v = 0.0f;
+#pragma unroll
+    for (int s = 0; s < SK; ++s) v += red[g * SK + s][r];
+    if constexpr (RESID) v += __half2float(R[row]);
+    y[row] = __float2half_rn(v);
+  }
+}
+
+template <int QT, bool RESID>
+int launch_gemv_q(const uint8_t* q, const __half* d, const __half* x, const __half* R, __half* y,
+                  int64_t N, int64_t K, cudaStream_t stream) {
+  // Two rows per warp group; K is split over two warps when a row has few blocks.
+  constexpr int RPW = 2;
+  const int64_t nblk = K / 32;
+  if (nblk <= 256) {
+    constexpr int SK = 2;
+    const unsigned grid = static_cast<unsigned>((N + (kQWarps / SK) * RPW - 1) / ((kQWarps / SK) * RPW));
+    B200_CUDA(launch_pdl(gemv_q_kernel<QT, RPW, SK, RESID>, dim3(grid), dim3(kQWarps * 32), 0,
+                         stream, q, d, x, R, y, N, K));
+  } else {
+    constexpr int SK = 1;
+    const unsigned grid = static_cast<unsigned>((N + (kQWarps / SK) * RPW - 1) / ((kQWarps / SK) * RPW));
+    B200_CUDA(launch_pdl(gemv_q_kernel<QT, RPW, SK, RESID>, dim3(grid), dim3(kQWarps * 32), 0,
+                         stream, q, d, x, R, y, N, K));
+  }
+  return ENGINE_OK;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int engine_cuda_quant_repack(int qtype, const void* blocks, void* q_out,
+                             engine_half_t* scales_out, int64_t N, int64_t K,
+                             engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(qtype == ENGINE_Q8_0 || qtype == ENGINE_Q4_0,
+               "quant_repack: qtype must be ENGINE_Q8_0 or ENGINE_Q4_0");
+  B200_REQUIRE(N >= 0 && K >= 0, "quant_repack: negative dimension");
+  B200_REQUIRE(K % 32 == 0, "quant_repack: K must be a multiple of the 32-element block");
+  B200_REQUIRE(blocks != nullptr && q_out != nullptr && scales_out != nullptr,
+               "quant_repack: null device pointer");
+  if (N == 0 || K == 0) return ENGINE_OK;
+  const int64_t nblk = K / 32;
+  const int64_t total = N * nblk;
+  const int64_t g64 = (total + 255) / 256;
+  const unsigned grid = static_cast<unsigned>(g64 < 65535 * 8 ? g64 : 65535 * 8);
+  const auto* in = static_cast<const uint8_t*>(blocks);
+  auto* q = static_cast<uint8_t*>(q_out);
+  auto* d = reinterpret_cast<__half*>(scales_out);
+  auto st = static_cast<cudaStream_t>(stream);
+  if (qtype == ENGINE_Q8_0) {
+    B200_CUDA(launch_pdl(quant_repack_kernel<8>, dim3(grid), dim3(256), 0, st, in, q, d, N, nblk));
+  } else {
+    B200_CUDA(launch_pdl(quant_repack_kernel<4>, dim3(grid), dim3(256), 0, st, in, q, d, N, nblk));
+  }
+  return check_launch("quant_repack");
+  B200_ENTRY_END
+}
+
+int engine_cuda_gemv_q_nk(int qtype, const void* q, const engine_half_t* scales,
+                          const engine_half_t* x, const engine_half_t* residual, engine_half_t* y,
+                          int64_t N, int64_t K, engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(qtype == ENGINE_Q8_0 || qtype == ENGINE_Q4_0,
+               "gemv_q_nk: qtype must be ENGINE_Q8_0 or ENGINE_Q4_0");
+  B200_REQUIRE(N >= 0 && K >= 0, "gemv_q_nk: dimensions must be non-negative");
+  B200_REQUIRE(K % 32 == 0, "gemv_q_nk: K must be a multiple of the 32-element block");
+  B200_REQUIRE(q != nullptr && scales != nullptr && x != nullptr && y != nullptr,
+               "gemv_q_nk: null device pointer");
+  if (N == 0) return ENGINE_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {  // empty rows: y = residual, or zeros
+    if (residual != nullptr) {
+      B200_CUDA(cudaMemcpyAsync(y, residual, static_cast<size_t>(N) * 2, cudaMemcpyDeviceToDevice, st));
+    } else {
+      B200_CUDA(cudaMemsetAsync(y, 0, static_cast<size_t>(N) * 2, st));
+    }
+    return ENGINE_OK;
+  }
+  B200_REQUIRE(reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0,
+               "gemv_q_nk: payload and x must be 16-byte aligned");
+  const auto* qq = static_cast<const uint8_t*>(q);
+  const auto* d = reinterpret_cast<const __half*>(scales);
+  const auto* xx = reinterpret_cast<const __half*>(x);
+  const auto* r = reinterpret_cast<const __half*>(residual);
+  auto* yy = reinterpret_cast<__half*>(y);
+  int rc;
+  if (qtype == ENGINE_Q8_0) {
+    rc = r ? launch_gemv_q<8, true>(qq, d, xx, r, yy, N, K, st)
+           : launch_gemv_q<8, false>(qq, d, xx, r, yy, N, K, st);
+  } else {
+    rc = r ? launch_gemv_q<4, true>(qq, d, xx, r, yy, N, K, st)
+           : launch_gemv_q<4, false>(qq, d, xx, r, yy, N, K, st);
+  }
+  if (rc != ENGINE_OK) return rc;
+  return check_launch("gemv_q_nk");
+  B200_ENTRY_END
+}
+
+}  // extern "C"

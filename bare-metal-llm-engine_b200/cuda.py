@@ -100,6 +100,21 @@ def rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps, stream=0)
                                                         _s(stream)))
 
 
+# ------------------------------------------------- block-quantised weights
+# engine_cuda_quant_repack / engine_cuda_gemv_q_nk: GGUF Q8_0 / Q4_0 blocks, the
+# formats the engine declares (include/engine/dtype.hpp:95-125).
+
+Q8_0, Q4_0 = 8, 4
+
+
+def quant_repack(qtype, blocks, q_out, scales_out, N, K, stream=0):
+    _check(lib().engine_cuda_quant_repack(qtype, blocks, q_out, scales_out, N, K, _s(stream)))
+
+
+def gemv_q_nk(qtype, q, scales, x, residual, y, N, K, stream=0):
+    _check(lib().engine_cuda_gemv_q_nk(qtype, q, scales, x, residual, y, N, K, _s(stream)))
+
+
 # ------------------------------------------------- tensor-parallel communicator
 # engine_tp_* (include/engine_b200.h): no counterpart in the reference.
 

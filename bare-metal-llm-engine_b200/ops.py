@@ -115,6 +115,30 @@ def rmsnorm_linear_swiglu(x, gamma, W_gu, eps: float = 1e-5, out=None):
     return Y
 
 
+def quant_repack(qtype, blocks, N, K):
+    """Packed GGUF blocks (uint8 CUDA tensor) -> (payload, scales) in the layout
+    gemv_q streams: payload [N, K] int8 (Q8_0) or [N, K/2] uint8 (Q4_0), scales
+    [N, K/32] FP16."""
+    _req(blocks, torch.uint8, "blocks")
+    pay = K if qtype == _c.Q8_0 else K // 2
+    q = torch.empty(N, pay, device=blocks.device, dtype=torch.uint8)
+    d = torch.empty(N, K // 32, device=blocks.device, dtype=torch.float16)
+    _c.quant_repack(qtype, blocks.data_ptr(), q.data_ptr(), d.data_ptr(), N, K, _stream())
+    return q, d
+
+
+def gemv_q(qtype, q, scales, x, residual=None, out=None):
+    """y = W x (+ residual) for W given by quant_repack's (payload, scales)."""
+    _req(q, torch.uint8, "q")
+    _req(scales, torch.float16, "scales")
+    _req(x, torch.float16, "x")
+    N, K = scales.shape[0], x.numel()
+    y = out if out is not None else torch.empty(N, device=x.device, dtype=torch.float16)
+    _c.gemv_q_nk(qtype, q.data_ptr(), scales.data_ptr(), x.data_ptr(), _ptr(residual),
+                 y.data_ptr(), N, K, _stream())
+    return y
+
+
 def swiglu(gate, up, out=None):
     _req(gate, torch.float16, "gate")
     _req(up, torch.float16, "up")

@@ -357,6 +357,23 @@ def secondary_configs(torch, pkg, dev, g, world, args):
         byt = 2.0 * (N * K + K + N)
         out[f"gemv_{N}x{K}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9}
         del sets
+    # Block-quantised decode GEMV (GGUF Q8_0 / Q4_0, the engine's declared formats),
+    # 4096x14336, in the streamed layout; random payload bytes and scales (timing
+    # only: the same bytes and work as real quantised weights).
+    N, K = 4096, 14336
+    for qtype, name, pay, nsets in ((8, "q8_0", K, 4), (4, "q4_0", K // 2, 6)):
+        sets = [(torch.randint(0, 256, (N, pay), device=dev, generator=g, dtype=torch.uint8),
+                 (torch.rand(N, K // 32, device=dev, generator=g) * 1e-3).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        fn = lambda s, st, qt=qtype: pkg.cuda.gemv_q_nk(  # noqa: E731
+            qt, s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0, s[3].data_ptr(), N, K, st)
+        ms = time_graph(torch, fn, sets, 60, 5)
+        byt = N * pay + 2.0 * (N * K // 32) + 2.0 * (K + N)
+        out[f"gemv_{name}_{N}x{K}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9,
+                                        "bytes_per_launch": byt}
+        del sets
+    torch.cuda.empty_cache()
     # Config 4a in BF16
     n = 4096
     sets = [(torch.randn(n, n, device=dev, generator=g).bfloat16(),

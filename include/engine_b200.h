@@ -197,6 +197,33 @@ ENGINE_B200_API int engine_cuda_embedding_f16(const engine_half_t* table, const 
                               int64_t vocab, engine_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Block-quantised decode GEMV.  The reference declares the formats but has no
+ * kernel for them (include/engine/dtype.hpp:95-125: GGUF's 32-element blocks
+ * with one FP16 scale):
+ *   ENGINE_Q8_0  { half d; int8 q[32]; }     34 bytes/block, w = d * q
+ *   ENGINE_Q4_0  { half d; uint8 nib[16]; }  18 bytes/block, w[j] = d * (lo(nib[j]) - 8),
+ *                                            w[j+16] = d * (hi(nib[j]) - 8)
+ * ------------------------------------------------------------------------- */
+#define ENGINE_Q8_0 8
+#define ENGINE_Q4_0 4
+
+/* Converts W[N,K] stored as packed GGUF blocks (row-major, K/32 blocks per row)
+ * into the layout engine_cuda_gemv_q_nk streams: q_out [N][K] int8 (Q8_0) or
+ * [N][K/2] bytes (Q4_0, each block's 16 bytes in GGUF order), and scales_out
+ * [N][K/32] FP16.  Run once when the weights are loaded.  K % 32 == 0. */
+ENGINE_B200_API int engine_cuda_quant_repack(int qtype, const void* blocks, void* q_out,
+                                             engine_half_t* scales_out, int64_t N, int64_t K,
+                                             engine_stream_t stream);
+
+/* y[N] = W x (+ residual) for W in the repacked block-quantised layout; FP16 x,
+ * y; FP32 accumulation.  The quantised form of gemv_f16_nk (kernels.hpp:120).
+ * q and x 16-byte aligned; K % 32 == 0. */
+ENGINE_B200_API int engine_cuda_gemv_q_nk(int qtype, const void* q, const engine_half_t* scales,
+                                          const engine_half_t* x, const engine_half_t* residual,
+                                          engine_half_t* y, int64_t N, int64_t K,
+                                          engine_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Tensor-parallel communicator over NVLink peer memory.  No counterpart in the
  * reference (it has no multi-GPU code): these replace the NCCL all-reduce (sum,
  * FP16) that follows the row-split O and down projections of the

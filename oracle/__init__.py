@@ -61,6 +61,8 @@ def _load_oracle():
         "orc_rmsnorm_linear_f16": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _f]),
         "orc_rmsnorm_linear_f16_mt": (None, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _f, _i]),
         "orc_swiglu_f16": (None, [_p, _p, _p, _i64]),
+        "orc_dequant_q": (None, [_i, _p, _p, _i64, _i64]),
+        "orc_gemv_q": (None, [_i, _p, _p, _p, _p, _p, _i64, _i64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -244,6 +246,38 @@ def swiglu_f16(gate, up):
     out = np.empty(g.shape, np.uint16)
     lib().orc_swiglu_f16(_ptr(g), _ptr(u), _ptr(out), g.size)
     return out.view(np.float16)
+
+
+# ---------------------------------------------------------- block-quantised
+
+Q8_0, Q4_0 = 8, 4
+
+
+def q_block_bytes(qtype: int) -> int:
+    """Bytes of one 32-element block, FP16 scale included (34 for Q8_0, 18 for Q4_0)."""
+    return 2 + (32 if qtype == Q8_0 else 16)
+
+
+def dequant_q(qtype, blocks, N, K):
+    """float32 W[N,K] from packed GGUF blocks (uint8 array of N*K/32 blocks)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    w = np.empty((N, K), np.float32)
+    lib().orc_dequant_q(int(qtype), _ptr(b), _ptr(w), N, K)
+    return w
+
+
+def gemv_q(qtype, blocks, x, residual=None, want_f32=False):
+    """y[N] = W x (+ residual) for W as packed blocks; FP64 accumulation, FP16 out."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    x = _bits(x)
+    R = _bits(residual)
+    K = x.size
+    N = b.size // (K // 32 * q_block_bytes(qtype))
+    y = np.empty(N, np.uint16)
+    y32 = np.empty(N, np.float32) if want_f32 else None
+    lib().orc_gemv_q(int(qtype), _ptr(b), _ptr(x), _ptr(R), _ptr(y), _ptr(y32), N, K)
+    y = y.view(np.float16)
+    return (y, y32) if want_f32 else y
 
 
 # ---------------------------------------------------------- derived bounds

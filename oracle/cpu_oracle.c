@@ -403,3 +403,57 @@ void orc_rmsnorm_linear_mt(const float* in, const float* rms_weight, const float
   orc_job j = {4, in, rms_weight, W, NULL, out, NULL, 0, 0, N, K, eps, 0};
   run_rows(j, M, nthreads);
 }
+
+/* ---------------------------------------------------------------- block-quantised
+ * The engine declares GGUF's block formats but implements neither a kernel nor
+ * a CPU path for them (include/engine/dtype.hpp:95-125, kQuantBlockSize = 32, one
+ * FP16 scale per block).  This is a restatement of the published format:
+ *   qtype 8 (Q8_0): block = { uint16 d; int8 q[32] }      34 bytes, w = d * q
+ *   qtype 4 (Q4_0): block = { uint16 d; uint8 nib[16] }   18 bytes,
+ *                   w[j] = d * ((nib[j] & 15) - 8), w[j+16] = d * ((nib[j] >> 4) - 8)
+ * Blocks are packed back to back, row-major (K/32 blocks per row); d is stored
+ * little-endian.  A dequantised weight d * q is exact in float (an 11-bit
+ * significand times an integer of at most 8 bits).  It is then accumulated
+ * against x in double, like the other oracle dot products. */
+
+static int orc_q_payload(int qtype) { return qtype == 8 ? 32 : 16; }
+
+/* w[N*K] (float) from the packed blocks. */
+void orc_dequant_q(int qtype, const uint8_t* blocks, float* w, int64_t N, int64_t K) {
+  const int pay = orc_q_payload(qtype);
+  const int64_t nblk = K / 32;
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t b = 0; b < nblk; ++b) {
+      const uint8_t* blk = blocks + (n * nblk + b) * (2 + pay);
+      const float d = orc_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+      float* out = w + n * K + b * 32;
+      if (qtype == 8) {
+        for (int i = 0; i < 32; ++i) out[i] = d * (float)(int8_t)blk[2 + i];
+      } else {
+        for (int j = 0; j < 16; ++j) {
+          out[j] = d * (float)((int)(blk[2 + j] & 15) - 8);
+          out[j + 16] = d * (float)((int)(blk[2 + j] >> 4) - 8);
+        }
+      }
+    }
+  }
+}
+
+/* y[n] = fp16( sum_k w[n,k] * x[k] (+ residual[n]) ), FP64 accumulation in
+ * increasing k; y32 (optional) receives the unrounded value as float. */
+void orc_gemv_q(int qtype, const uint8_t* blocks, const uint16_t* x, const uint16_t* residual,
+                uint16_t* y, float* y32, int64_t N, int64_t K) {
+  const int pay = orc_q_payload(qtype);
+  const int64_t nblk = K / 32;
+  float w[32];
+  for (int64_t n = 0; n < N; ++n) {
+    double acc = 0.0;
+    for (int64_t b = 0; b < nblk; ++b) {
+      orc_dequant_q(qtype, blocks + (n * nblk + b) * (2 + pay), w, 1, 32);
+      for (int i = 0; i < 32; ++i) acc += (double)w[i] * (double)orc_f16_to_f32(x[b * 32 + i]);
+    }
+    if (residual) acc += (double)orc_f16_to_f32(residual[n]);
+    if (y32) y32[n] = (float)acc;
+    y[n] = orc_f32_to_f16((float)acc);
+  }
+}

@@ -189,3 +189,17 @@ def test_fused_swiglu_entry_rejects_bad_arguments(pkg):
     # empty work is a no-op (nothing is launched), gamma may be null
     c.rmsnorm_linear_swiglu_f16(P, 0, P, P, 0, 4, 4, 1e-5)
     c.rmsnorm_linear_swiglu_f16(P, 0, P, P, 2, 0, 4, 1e-5)
+
+
+def test_quant_entries_reject_bad_arguments(pkg):
+    c = pkg.cuda
+    _throws(pkg, c.quant_repack, 5, P, P, P, 4, 32, substr="qtype")
+    _throws(pkg, c.quant_repack, 8, P, P, P, -1, 32, substr="negative")
+    _throws(pkg, c.quant_repack, 8, P, P, P, 4, 48, substr="multiple")
+    _throws(pkg, c.quant_repack, 4, 0, P, P, 4, 32, substr="null")
+    _throws(pkg, c.gemv_q_nk, 5, P, P, P, 0, P, 4, 32, substr="qtype")
+    _throws(pkg, c.gemv_q_nk, 8, P, P, P, 0, P, -4, 32, substr="non-negative")
+    _throws(pkg, c.gemv_q_nk, 8, P, P, P, 0, P, 4, 40, substr="multiple")
+    _throws(pkg, c.gemv_q_nk, 4, P, 0, P, 0, P, 4, 32, substr="null")
+    c.gemv_q_nk(8, P, P, P, 0, P, 0, 32)   # N == 0: no-op
+    c.quant_repack(4, P, P, P, 0, 32)      # no rows: no-op
