@@ -83,7 +83,7 @@ __device__ __forceinline__ float block_dot(const uint4 (&p)[2], const uint4 (&xv
 }
 
 template <int QT, int RPW, int SK, bool RESID>
-__global__ void __launch_bounds__(kQWarps * 32) gemv_q_kernel(
+__global__ void __launch_bounds__(kQWarps * 32, 2) gemv_q_kernel(
     const uint8_t* __restrict__ q, const __half* __restrict__ d, const __half* __restrict__ x,
     const __half* __restrict__ R, __half* __restrict__ y, int64_t N, int64_t K) {
   constexpr int GROUPS = kQWarps / SK;
@@ -115,22 +115,53 @@ __global__ void __launch_bounds__(kQWarps * 32) gemv_q_kernel(
   float acc[RPW];
 #pragma unroll
   for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
-  if (row0 < N) {
-#pragma unroll 2
-    for (int64_t b = b0; b < nblk; b += kStride) {
-      uint4 p[RPW][2];
-      float sc[RPW];
+  // Software pipeline: U blocks per lane per buffer, two buffers -- the next U
+  // blocks' payload and scales are in flight while the current U are multiplied
+  // (about 256 payload bytes per lane in flight, as in the FP16 decode GEMV).
+  constexpr int U = QT == 8 ? 2 : 4;
+  constexpr int NP = QT == 8 ? 2 : 1;  // 16-byte payload words per block
+  uint4 pa[U][RPW][NP], pb[U][RPW][NP];
+  float sa[U][RPW], sb[U][RPW];
+  auto load = [&](int64_t bb, uint4 (&p)[U][RPW][NP], float (&sc)[U][RPW]) {
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        p[r][0] = ld_stream_v4(prow[r] + b * PAY);
-        p[r][1] = (QT == 8) ? ld_stream_v4(prow[r] + b * PAY + 16) : make_uint4(0, 0, 0, 0);
-        sc[r] = __half2float(drow[r][b]);
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = bb + kStride * u;
+      if (b < nblk) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+          for (int w = 0; w < NP; ++w) p[u][r][w] = ld_stream_v4(prow[r] + b * PAY + 16 * w);
+          sc[u][r] = __half2float(drow[r][b]);
+        }
       }
-      uint4 xv[4];
+    }
+  };
+  auto compute = [&](int64_t bb, uint4 (&p)[U][RPW][NP], float (&sc)[U][RPW]) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) xv[c] = __ldg(reinterpret_cast<const uint4*>(x + 32 * b) + c);
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = bb + kStride * u;
+      if (b < nblk) {
+        uint4 xv[4];
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) acc[r] = fmaf(sc[r], block_dot<QT>(p[r], xv), acc[r]);
+        for (int c = 0; c < 4; ++c) xv[c] = __ldg(reinterpret_cast<const uint4*>(x + 32 * b) + c);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          uint4 pp[2];
+          pp[0] = p[u][r][0];
+          pp[1] = p[u][r][NP - 1];
+          acc[r] = fmaf(sc[u][r], block_dot<QT>(pp, xv), acc[r]);
+        }
+      }
+    }
+  };
+  if (row0 < N) {
+    int64_t b = b0;
+    load(b, pa, sa);
+    for (; b < nblk; b += 2 * kStride * U) {
+      load(b + kStride * U, pb, sb);
+      compute(b, pa, sa);
+      load(b + 2 * kStride * U, pa, sa);
+      compute(b + kStride * U, pb, sb);
     }
   }
 #pragma unroll
