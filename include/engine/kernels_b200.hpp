@@ -169,6 +169,23 @@ inline void embedding_fp16(const __half* table, const std::int32_t* ids, __half*
                                                num_tokens, hidden, vocab, stream));
 }
 
+// Block-quantised weights (DType::Q8_0 / DType::Q4_0, dtype.hpp:95-125): split
+// GGUF's packed blocks once at load time, then run the decode GEMV over the
+// split layout.  qtype is ENGINE_Q8_0 or ENGINE_Q4_0; K % 32 == 0.
+inline void quant_repack(int qtype, const void* blocks, void* payload, __half* scales,
+                         std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
+  b200_detail::check(
+      engine_cuda_quant_repack(qtype, blocks, payload, b200_detail::h(scales), N, K, stream));
+}
+
+inline void gemv_q_nk(int qtype, const void* payload, const __half* scales, const __half* x,
+                      const __half* residual, __half* y, std::int64_t N, std::int64_t K,
+                      cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_gemv_q_nk(qtype, payload, b200_detail::h(scales),
+                                           b200_detail::h(x), b200_detail::h(residual),
+                                           b200_detail::h(y), N, K, stream));
+}
+
 // -- tensor-parallel communicator (engine_tp_*) --------------------------------
 // One per rank, on the rank's current device.  The host exchanges handle()
 // between the ranks (all-gather), then calls open() with all of them in rank
