@@ -51,32 +51,66 @@ __global__ void quant_repack_kernel(const uint8_t* __restrict__ blocks, uint8_t*
   }
 }
 
+// Integer weights become FP16 halves without an int->float conversion (the
+// magic-number method; for 4-bit nibbles the LOP3 form of Kim et al., "Who Says
+// Elephants Can't Run?", 2022): a value u < 1024 placed in the mantissa of
+// 0x6400 (1024.0) reads as 1024 + u, and one f16x2 subtract (or, for a nibble
+// in bits 4-7, one f16x2 fma by 1/16) leaves the signed weight exactly.
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b),
+                      *reinterpret_cast<const __half2*>(&c));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// s += q.lo * x.lo; s += q.hi * x.hi -- sm_100 mixed-precision fma: FP16 inputs,
+// FP32 accumulator, one rounding (the product of two halves is exact in FP32, so
+// this equals fmaf(float(q), float(x), s)).
+__device__ __forceinline__ void fma_h2(float& s, uint32_t q2, uint32_t x2) {
+  asm("{\n .reg .f16 ql, qh, xl, xh;\n mov.b32 {ql, qh}, %1;\n mov.b32 {xl, xh}, %2;\n"
+      " fma.rn.f32.f16 %0, ql, xl, %0;\n fma.rn.f32.f16 %0, qh, xh, %0;\n}"
+      : "+f"(s) : "r"(q2), "r"(x2));
+}
+
 /// sum_i q_i * x_i over one block; xv = the block's 32 x values (4 x uint4).
 template <int QT>
 __device__ __forceinline__ float block_dot(const uint4 (&p)[2], const uint4 (&xv)[4]) {
-  float xf[32];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    float t[8];
-    h8_to_f8(xv[c], t);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xf[8 * c + i] = t[i];
-  }
+  const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[0]);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&p[0]);
   float s = 0.0f;
   if constexpr (QT == 8) {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&p[0]);  // 8 words = 32 int8
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int v = static_cast<int8_t>((w[i >> 2] >> (8 * (i & 3))) & 0xffu);
-      s = fmaf(static_cast<float>(v), xf[i], s);
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t u = w[k] ^ 0x80808080u;
+      const uint32_t q01 = h2_sub(__byte_perm(u, 0x64646464u, 0x4140), 0x64806480u);
+      const uint32_t q23 = h2_sub(__byte_perm(u, 0x64646464u, 0x4342), 0x64806480u);
+      fma_h2(s, q01, xw[2 * k]);
+      fma_h2(s, q23, xw[2 * k + 1]);
     }
   } else {
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(&p[0]);  // 4 words = 16 bytes
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t byte = (w[j >> 2] >> (8 * (j & 3))) & 0xffu;
-      s = fmaf(static_cast<float>(static_cast<int>(byte & 0xfu) - 8), xf[j], s);
-      s = fmaf(static_cast<float>(static_cast<int>(byte >> 4) - 8), xf[j + 16], s);
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t v0 = w[m];
+      const uint32_t v1 = w[m] >> 8;
+      const uint32_t a = h2_sub((v0 & 0x000f000fu) | 0x64006400u, 0x64086408u);
+      const uint32_t b = h2_fma((v0 & 0x00f000f0u) | 0x64006400u, 0x2c002c00u, 0xd480d480u);
+      const uint32_t c = h2_sub((v1 & 0x000f000fu) | 0x64006400u, 0x64086408u);
+      const uint32_t e = h2_fma((v1 & 0x00f000f0u) | 0x64006400u, 0x2c002c00u, 0xd480d480u);
+      const uint32_t x01 = xw[2 * m], x23 = xw[2 * m + 1];
+      const uint32_t y01 = xw[8 + 2 * m], y23 = xw[9 + 2 * m];
+      asm("{\n .reg .f16 al, ah, bl, bh, cl, chh, el, eh, x0, x1, x2, x3, y0, y1, y2, y3;\n"
+          " mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n mov.b32 {cl, chh}, %3;\n"
+          " mov.b32 {el, eh}, %4;\n mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n"
+          " mov.b32 {y0, y1}, %7;\n mov.b32 {y2, y3}, %8;\n"
+          " fma.rn.f32.f16 %0, al, x0, %0;\n fma.rn.f32.f16 %0, bl, y0, %0;\n"
+          " fma.rn.f32.f16 %0, cl, x1, %0;\n fma.rn.f32.f16 %0, el, y1, %0;\n"
+          " fma.rn.f32.f16 %0, ah, x2, %0;\n fma.rn.f32.f16 %0, bh, y2, %0;\n"
+          " fma.rn.f32.f16 %0, chh, x3, %0;\n fma.rn.f32.f16 %0, eh, y3, %0;\n}"
+          : "+f"(s)
+          : "r"(a), "r"(b), "r"(c), "r"(e), "r"(x01), "r"(x23), "r"(y01), "r"(y23));
     }
   }
   return s;

@@ -117,8 +117,8 @@ def rmsnorm_linear_swiglu(x, gamma, W_gu, eps: float = 1e-5, out=None):
 
 def quant_repack(qtype, blocks, N, K):
     """Packed GGUF blocks (uint8 CUDA tensor) -> (payload, scales) in the layout
-    gemv_q streams: payload [N, K] int8 (Q8_0) or [N, K/2] uint8 (Q4_0), scales
-    [N, K/32] FP16."""
+    gemv_q streams: payload [N, K] int8 (Q8_0) or [N, K/2] uint8 (Q4_0, each
+    block's 16 nibble bytes in GGUF order), scales [N, K/32] FP16."""
     _req(blocks, torch.uint8, "blocks")
     pay = K if qtype == _c.Q8_0 else K // 2
     q = torch.empty(N, pay, device=blocks.device, dtype=torch.uint8)

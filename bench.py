@@ -552,7 +552,8 @@ def run_headline(args):
 
 
 KERNEL_CASES = ("gemm4096", "gemv_4096x14336", "rmsnorm_qkv_b1", "rmsnorm_qkv_b16",
-                "matmul_f32_512", "prefill_s2048", "gate_up_swiglu_b1", "tp_down_b1_world1")
+                "matmul_f32_512", "prefill_s2048", "gate_up_swiglu_b1", "tp_down_b1_world1",
+                "gemv_q8_0_4096x14336", "gemv_q4_0_4096x14336")
 
 
 def run_kernel_case(args) -> int:
@@ -610,6 +611,16 @@ def run_kernel_case(args) -> int:
                  torch.empty(1, N, device=dev, dtype=torch.float16)) for _ in range(4)]
         fn = lambda s: pkg.cuda.tp_linear_allreduce_f16(comm.handle, s[0].data_ptr(), s[1].data_ptr(),  # noqa: E731
                                                         s[2].data_ptr(), s[3].data_ptr(), 1, N, K, st)
+    elif c.startswith("gemv_q"):  # block-quantised decode GEMV, streamed layout (timing only)
+        N, K = 4096, 14336
+        qt = 8 if c.startswith("gemv_q8") else 4
+        pay = K if qt == 8 else K // 2
+        sets = [(torch.randint(0, 256, (N, pay), device=dev, generator=g, dtype=torch.uint8),
+                 (torch.rand(N, K // 32, device=dev, generator=g) * 1e-3).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.gemv_q_nk(qt, s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0,  # noqa: E731
+                                          s[3].data_ptr(), N, K, st)
     else:  # prefill_s2048
         S, N, K = 2048, 14336, 4096
         sets = [(torch.randn(S, K, device=dev, generator=g).half(),

@@ -1,12 +1,14 @@
 """GPU: block-quantised decode GEMV (GGUF Q8_0 / Q4_0) through the C ABI.
 
-engine_cuda_quant_repack must split packed blocks into (payload, scales)
-exactly as the numpy restatement does.  engine_cuda_gemv_q_nk must match the
-oracle's FP64 GEMV on the same blocks within the derived bound for FP32
-accumulation and one FP16 output rounding (tests/bounds.py gemv16_bound, with
-sum |w||x| over the dequantised weights).  The shapes cover ragged N, the
-K-split and whole-row warp paths (K/32 <= 256 and > 256), the residual, and
-K = 0.
+engine_cuda_quant_repack must split packed blocks into (payload, scales) in
+the streamed layout exactly as the numpy restatement (quant_np.split) does.
+engine_cuda_gemv_q_nk must match the oracle's FP64 GEMV on the same blocks
+within the derived bound for FP32 accumulation and one FP16 output rounding
+(tests/bounds.py gemv16_bound, with sum |w||x| over the dequantised weights).
+The shapes cover the K-split and whole-row warp paths (K <= 8192 and > 8192:
+K = 32, 64, 4096, 8192 + 96, 14336, 65536 + 256), ragged N, several rows per
+warp group past N, with and without a residual, an all-zero block, the
+4096x14336 decode shape, and K = 0.
 """
 from __future__ import annotations
 
@@ -28,10 +30,13 @@ def _dev(a, dev):
 
 @pytest.mark.parametrize("qtype", [qn.Q8_0, qn.Q4_0])
 @pytest.mark.parametrize("N,K,resid", [(4096, 4096, False), (1000, 4096, True), (300, 14336, True),
-                                       (64, 32, False), (5, 64, True)])
+                                       (64, 32, False), (5, 64, True), (4096, 14336, False),
+                                       (33, 8192 + 96, True), (14336, 4096, True),
+                                       (64, 65536 + 256, False)])
 def test_gemv_q_matches_oracle(pkg, dev, qtype, N, K, resid):
     rng = np.random.default_rng(N + K + qtype)
     W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    W[N // 2, :32] = 0.0  # an all-zero block: scale 0
     x = rng.standard_normal(K).astype(np.float16)
     R = rng.standard_normal(N).astype(np.float16) if resid else None
     blocks = qn.quantize(qtype, W)
