@@ -46,6 +46,7 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_gemv": [_p, _p, _p, _i64, _i64, _p],
     "engine_cuda_gemv_fp16": [_p, _p, _p, _i64, _i64, _p],
     "engine_cuda_rmsnorm": [_p, _p, _p, _i64, _i64, _f, _p],
+    "engine_cuda_residual_rmsnorm": [_p, _p, _p, _p, _p, _i64, _i64, _f, _p],
     "engine_cuda_rmsnorm_linear": [_p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_rmsnorm_linear_fused_direct": [_p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
     "engine_cuda_vector_add": [_p, _p, _p, _i64, _p],

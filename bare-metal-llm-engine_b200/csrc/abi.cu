@@ -222,18 +222,31 @@ namespace {
 // One block per row (grid-stride over rows).  Squares are summed in double and
 // the scale is formed as float(1 / sqrt(mean + eps)) in double, the reference's
 // arithmetic (src/cpu_ref/rmsnorm_cpu.cpp:19-43); out = (x * scale) * w in float.
+// RES: the row is first s = x + residual in float, written to sum_out and
+// normalised in place of x (src/cpu_ref/residual_rmsnorm_cpu.cpp:19-51).  Each
+// thread reads back in the second pass only the sum_out elements it wrote.
+template <bool RES>
 __global__ void __launch_bounds__(256) rmsnorm_f32_kernel(const float* __restrict__ in,
+                                                          const float* __restrict__ res,
                                                           const float* __restrict__ w,
                                                           float* __restrict__ out,
+                                                          float* __restrict__ sum_out,
                                                           int64_t rows, int64_t cols,
                                                           float eps) {
   __shared__ double s_part[8];
   __shared__ float s_scale;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* src = in + r * cols;
+    const float* rsrc = RES ? res + r * cols : nullptr;
+    float* ssum = RES ? sum_out + r * cols : nullptr;
     double ss = 0.0;
     for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
-      const double v = static_cast<double>(src[c]);
+      float x = src[c];
+      if constexpr (RES) {
+        x = __fadd_rn(x, rsrc[c]);
+        ssum[c] = x;
+      }
+      const double v = static_cast<double>(x);
       ss = __dadd_rn(ss, __dmul_rn(v, v));
     }
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(256) rmsnorm_f32_kernel(const float* __restric
     float* dst = out + r * cols;
     for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
       const float wv = w ? w[c] : 1.0f;
-      dst[c] = __fmul_rn(__fmul_rn(src[c], scale), wv);
+      dst[c] = __fmul_rn(__fmul_rn(RES ? ssum[c] : src[c], scale), wv);
     }
     __syncthreads();
   }
@@ -342,8 +355,26 @@ int engine_cuda_rmsnorm(const float* in, const float* weight, float* out, int64_
   if (rows == 0 || cols == 0) return ENGINE_OK;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
   const int grid = static_cast<int>(rows < cap ? rows : cap);
-  rmsnorm_f32_kernel<<<grid, 256, 0, stream>>>(in, weight, out, rows, cols, eps);
+  rmsnorm_f32_kernel<false><<<grid, 256, 0, stream>>>(in, nullptr, weight, out, nullptr, rows,
+                                                       cols, eps);
   return check_launch("rmsnorm");
+  B200_ENTRY_END
+}
+
+int engine_cuda_residual_rmsnorm(const float* x, const float* residual, const float* weight,
+                                 float* norm_out, float* sum_out, int64_t rows, int64_t cols,
+                                 float eps, engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(rows >= 0 && cols >= 0, "residual_rmsnorm: negative dimension");
+  B200_REQUIRE(x != nullptr && residual != nullptr && norm_out != nullptr && sum_out != nullptr,
+               "residual_rmsnorm: null device pointer");
+  B200_REQUIRE(eps >= 0.0f, "residual_rmsnorm: eps must be non-negative");
+  if (rows == 0 || cols == 0) return ENGINE_OK;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
+  const int grid = static_cast<int>(rows < cap ? rows : cap);
+  rmsnorm_f32_kernel<true><<<grid, 256, 0, stream>>>(x, residual, weight, norm_out, sum_out, rows,
+                                                      cols, eps);
+  return check_launch("residual_rmsnorm");
   B200_ENTRY_END
 }
 

@@ -38,6 +38,12 @@ def rmsnorm(inp, weight, out, rows, cols, eps, stream=0):  # kernels.hpp:62
     _check(lib().engine_cuda_rmsnorm(inp, weight, out, rows, cols, eps, _s(stream)))
 
 
+def residual_rmsnorm(x, residual, weight, norm_out, sum_out, rows, cols, eps,  # kernels.hpp:110
+                     stream=0):
+    _check(lib().engine_cuda_residual_rmsnorm(x, residual, weight, norm_out, sum_out, rows, cols,
+                                              eps, _s(stream)))
+
+
 def rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, stream=0):  # kernels.hpp:97
     _check(lib().engine_cuda_rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, _s(stream)))
 

@@ -139,6 +139,21 @@ def gemv_q(qtype, q, scales, x, residual=None, out=None):
     return y
 
 
+def residual_rmsnorm(x, residual, weight=None, eps: float = 1e-5):
+    """(norm_out, sum_out): sum_out = x + residual, norm_out = rmsnorm(sum_out) *
+    weight, FP32 [rows, cols] (engine::cuda::residual_rmsnorm)."""
+    _req(x, torch.float32, "x")
+    _req(residual, torch.float32, "residual")
+    if weight is not None:
+        _req(weight, torch.float32, "weight")
+    rows, cols = x.shape
+    norm = torch.empty_like(x)
+    sm = torch.empty_like(x)
+    _c.residual_rmsnorm(x.data_ptr(), residual.data_ptr(), _ptr(weight), norm.data_ptr(),
+                        sm.data_ptr(), rows, cols, eps, _stream())
+    return norm, sm
+
+
 def swiglu(gate, up, out=None):
     _req(gate, torch.float16, "gate")
     _req(up, torch.float16, "up")

@@ -57,6 +57,14 @@ inline void rmsnorm(const float* in, const float* weight, float* out, std::int64
   b200_detail::check(engine_cuda_rmsnorm(in, weight, out, rows, cols, eps, stream));
 }
 
+// kernels.hpp:110
+inline void residual_rmsnorm(const float* x, const float* residual, const float* weight,
+                             float* norm_out, float* sum_out, std::int64_t rows,
+                             std::int64_t cols, float eps, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_residual_rmsnorm(x, residual, weight, norm_out, sum_out, rows,
+                                                  cols, eps, stream));
+}
+
 inline void matmul_naive(const float* A, const float* B, float* C, std::int64_t M,
                          std::int64_t N, std::int64_t K, cudaStream_t stream = 0) {
   b200_detail::check(engine_cuda_matmul_naive(A, B, C, M, N, K, stream));

@@ -97,6 +97,15 @@ ENGINE_B200_API int engine_cuda_gemv_fp16(const engine_half_t* A, const engine_h
 ENGINE_B200_API int engine_cuda_rmsnorm(const float* in, const float* weight, float* out, int64_t rows,
                         int64_t cols, float eps, engine_stream_t stream);
 
+/* Fused residual add + RMSNorm: sum_out = x + residual, norm_out =
+ * rmsnorm(sum_out) * weight (weight may be null; x, residual, norm_out and
+ * sum_out may not).  kernels.hpp:110 (residual_rmsnorm), launcher
+ * kernels/residual_rmsnorm.cu:124-147. */
+ENGINE_B200_API int engine_cuda_residual_rmsnorm(const float* x, const float* residual,
+                                                 const float* weight, float* norm_out,
+                                                 float* sum_out, int64_t rows, int64_t cols,
+                                                 float eps, engine_stream_t stream);
+
 /* out[M,N] = rmsnorm(in[M,K], rms_weight, eps) * W[K,N]; rms_weight may be null.
  * kernels.hpp:97 (rmsnorm_linear).  One fused launch for every M. */
 ENGINE_B200_API int engine_cuda_rmsnorm_linear(const float* in, const float* rms_weight, const float* W,

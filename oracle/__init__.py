@@ -51,6 +51,7 @@ def _load_oracle():
         "orc_gemv": (None, [_p, _p, _p, _i64, _i64]),
         "orc_gemv_fp16": (None, [_p, _p, _p, _i64, _i64]),
         "orc_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f]),
+        "orc_residual_rmsnorm": (None, [_p, _p, _p, _p, _p, _i64, _i64, _f]),
         "orc_rmsnorm_linear": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f]),
         "orc_rmsnorm_linear_mt": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _i]),
         "orc_vector_add": (None, [_p, _p, _p, _i64]),
@@ -101,6 +102,7 @@ def ref_lib():
             "ref_gemv": (None, [_p, _p, _p, _i64, _i64]),
             "ref_gemv_fp16": (None, [_p, _p, _p, _i64, _i64]),
             "ref_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f]),
+            "ref_residual_rmsnorm": (None, [_p, _p, _p, _p, _p, _i64, _i64, _f]),
             "ref_rmsnorm_linear": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _i]),
             "ref_swiglu_fp16": (None, [_p, _p, _p, _i64]),
             "ref_vector_add": (None, [_p, _p, _p, _i64]),
@@ -166,6 +168,18 @@ def rmsnorm(x, w, eps):
     rows, cols = x.shape
     lib().orc_rmsnorm(_ptr(x), _ptr(w), _ptr(out), rows, cols, eps)
     return out
+
+
+def residual_rmsnorm(x, residual, w, eps):
+    """(norm_out, sum_out) of src/cpu_ref/residual_rmsnorm_cpu.cpp:19-51."""
+    x = _c(x, np.float32)
+    residual = None if residual is None else _c(residual, np.float32)
+    w = None if w is None else _c(w, np.float32)
+    norm = np.empty_like(x)
+    sm = np.empty_like(x)
+    rows, cols = x.shape
+    lib().orc_residual_rmsnorm(_ptr(x), _ptr(residual), _ptr(w), _ptr(norm), _ptr(sm), rows, cols, eps)
+    return norm, sm
 
 
 def rmsnorm_linear(x, w, W, eps, nthreads: int = 1):

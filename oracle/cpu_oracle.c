@@ -158,6 +158,34 @@ void orc_rmsnorm(const float* in, const float* weight, float* out, int64_t rows,
   }
 }
 
+/* sum_out = x + residual; norm_out = rmsnorm(sum_out) * weight.  Follows
+ * src/cpu_ref/residual_rmsnorm_cpu.cpp:19-51: the float sum, squares of it
+ * accumulated in double in increasing-c order, scale = float(1 / sqrt(mean +
+ * eps)) in double, norm = (s * scale) * w in float.  residual, weight and
+ * sum_out may be NULL, as in the reference. */
+void orc_residual_rmsnorm(const float* x, const float* residual, const float* weight,
+                          float* norm_out, float* sum_out, int64_t rows, int64_t cols,
+                          float eps) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* sx = x + r * cols;
+    const float* sr = residual ? residual + r * cols : NULL;
+    float* dn = norm_out + r * cols;
+    float* ds = sum_out ? sum_out + r * cols : NULL;
+    double sumsq = 0.0;
+    for (int64_t c = 0; c < cols; ++c) {
+      const float v = sx[c] + (sr ? sr[c] : 0.0f);
+      if (ds) ds[c] = v;
+      sumsq += (double)v * (double)v;
+    }
+    const float scale = (float)(1.0 / sqrt(sumsq / (double)cols + (double)eps));
+    for (int64_t c = 0; c < cols; ++c) {
+      const float v = ds ? ds[c] : sx[c] + (sr ? sr[c] : 0.0f);
+      const float w = weight ? weight[c] : 1.0f;
+      dn[c] = v * scale * w;
+    }
+  }
+}
+
 /* out[M,N] = rmsnorm(in)[M,K] * W[K,N].  Follows src/cpu_ref/rmsnorm_linear_cpu.cpp:18-51. */
 static void rmsnorm_linear_rows(const float* in, const float* rms_weight, const float* W,
                                 float* out, int64_t r0, int64_t r1, int64_t N, int64_t K,

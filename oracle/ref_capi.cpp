@@ -73,6 +73,12 @@ void ref_rmsnorm(const float* in, const float* weight, float* out, std::int64_t 
   engine::cpu::rmsnorm(in, weight, out, rows, cols, eps);
 }
 
+void ref_residual_rmsnorm(const float* x, const float* residual, const float* weight,
+                          float* norm_out, float* sum_out, std::int64_t rows, std::int64_t cols,
+                          float eps) {
+  engine::cpu::residual_rmsnorm(x, residual, weight, norm_out, sum_out, rows, cols, eps);
+}
+
 void ref_rmsnorm_linear(const float* in, const float* rms_weight, const float* W, float* out,
                         std::int64_t M, std::int64_t N, std::int64_t K, float eps,
                         int nthreads) {

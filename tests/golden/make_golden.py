@@ -6,8 +6,8 @@ The reference engine writes its golden data with ``tools/gen_reference.py``
 20260826)`` drawn in one sequence across all cases, ``gen_reference.py:58``).
 This script imports that generator read-only, runs it with its NumPy backend
 and, for every case on the matrix-multiply hot path (``matmul__*``,
-``gemv__*``, ``gemv_fp16__*``, ``rmsnorm_linear__*`` and the ``rmsnorm__*``
-dependency), records:
+``gemv__*``, ``gemv_fp16__*``, ``rmsnorm_linear__*``, the ``rmsnorm__*``
+dependency and the ``residual_rmsnorm__*`` epilogue), records:
 
 * the generator state immediately BEFORE the case's draws, so the inputs can be
   regenerated bit-for-bit anywhere NumPy is present (``golden.py`` replays the
@@ -32,7 +32,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-PREFIXES = ("matmul__", "gemv__", "gemv_fp16__", "rmsnorm_linear__", "rmsnorm__")
+PREFIXES = ("matmul__", "gemv__", "gemv_fp16__", "rmsnorm_linear__", "rmsnorm__",
+            "residual_rmsnorm__")
 
 
 def sha(a: np.ndarray) -> str:

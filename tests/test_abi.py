@@ -78,8 +78,11 @@ def test_launchers_reject_negative_dimensions(pkg):
     _throws(pkg, c.linear_f16, P, P, 0, P, -1, 4, 4, substr="non-negative")
     _throws(pkg, c.gemv_f16_nk, P, P, 0, P, -1, 4, substr="non-negative")
     _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, -1, 4, 1e-5, substr="negative")
+    _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, -1, 4, 1e-5, substr="negative")
+    _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, 4, -1, 1e-5, substr="negative")
     # eps < 0 would put a negative number under the square root.
     _throws(pkg, c.rmsnorm, P, P, P, 4, 4, -1.0, substr="eps")
+    _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, 4, 4, -1.0, substr="eps")
     _throws(pkg, c.rmsnorm_linear, P, P, P, P, 4, 4, 4, -1.0, substr="eps")
     _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, 4, 4, -1.0, substr="eps")
 
@@ -107,7 +110,13 @@ def test_launchers_reject_null_pointers(pkg):
     _throws(pkg, c.rmsnorm_linear_f16, P, P, 0, 0, P, 2, 2, 2, 1e-5, substr="null")
     _throws(pkg, c.swiglu_fp16, P, 0, P, 4, substr="null")
     _throws(pkg, c.vector_add, P, P, 0, 4, substr="null")
+    # residual_rmsnorm: every pointer but the weight (test_kernels.cu:1752-1758)
+    _throws(pkg, c.residual_rmsnorm, 0, P, P, P, P, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.residual_rmsnorm, P, 0, P, P, P, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.residual_rmsnorm, P, P, P, 0, P, 2, 2, 1e-5, substr="null")
+    _throws(pkg, c.residual_rmsnorm, P, P, P, P, 0, 2, 2, 1e-5, substr="null")
     # rms weight / gamma may be null: "no learned gain" is a valid configuration.
+    c.residual_rmsnorm(P, P, 0, P, P, 0, 0, 1e-5)
     c.rmsnorm(P, 0, P, 0, 0, 1e-5)
     c.rmsnorm_linear(P, 0, P, P, 0, 0, 0, 1e-5)
     c.rmsnorm_linear_f16(P, 0, P, 0, P, 0, 0, 0, 1e-5)
@@ -115,6 +124,8 @@ def test_launchers_reject_null_pointers(pkg):
 
 def test_empty_work_is_a_no_op_not_an_error(pkg):
     c = pkg.cuda
+    c.residual_rmsnorm(P, P, P, P, P, 0, 8, 1e-5)
+    c.residual_rmsnorm(P, P, P, P, P, 8, 0, 1e-5)
     c.rmsnorm(P, P, P, 0, 8, 1e-5)
     c.rmsnorm(P, P, P, 8, 0, 1e-5)
     c.matmul_naive(P, P, P, 0, 8, 8)

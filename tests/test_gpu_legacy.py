@@ -195,6 +195,56 @@ def test_rmsnorm_matches_reference(pkg, dev, stem):
     assert np.array_equal(got, oracle.rmsnorm(g["input"], w, EPS))
 
 
+@pytest.mark.parametrize("stem", [s for s in golden.stems("residual_rmsnorm__") if not s.endswith("zeros")])
+def test_residual_rmsnorm_matches_reference(pkg, dev, stem):
+    """test_kernels.cu:972-1010: norm and sum against the reference's golden data,
+    kRmsRtol / kRmsAtol; plus bit-identity with the oracle (same arithmetic)."""
+    g = golden.load(stem)
+    rows, cols = g["x"].shape
+    w = g.get("weight")
+    d_w = dev_t(w) if w is not None else None
+    norm = torch.zeros(rows, cols, device=dev)
+    sm = torch.zeros(rows, cols, device=dev)
+    pkg.cuda.residual_rmsnorm(dev_t(g["x"]).data_ptr(), dev_t(g["residual"]).data_ptr(),
+                              0 if d_w is None else d_w.data_ptr(), norm.data_ptr(),
+                              sm.data_ptr(), rows, cols, EPS)
+    got_norm, got_sum = host(norm), host(sm)
+    close(got_norm, g["expected"], 1e-5, 1e-6, stem + " (norm)")
+    close(got_sum, g["sum_out"], 1e-5, 1e-6, stem + " (sum)")
+    o_norm, o_sum = oracle.residual_rmsnorm(g["x"], g["residual"], w, EPS)
+    assert np.array_equal(got_sum, o_sum)
+    assert np.array_equal(got_norm, o_norm)
+
+
+def test_residual_rmsnorm_of_zeros_is_zeros_not_nan(pkg, dev):
+    """test_kernels.cu:1012-1050: outputs pre-filled with NaN must become exact zeros."""
+    g = golden.load("residual_rmsnorm__zeros")
+    rows, cols = 2, 256
+    norm = torch.full((rows, cols), float("nan"), device=dev)
+    sm = torch.full((rows, cols), float("nan"), device=dev)
+    pkg.cuda.residual_rmsnorm(dev_t(g["x"]).data_ptr(), dev_t(g["residual"]).data_ptr(), 0,
+                              norm.data_ptr(), sm.data_ptr(), rows, cols, EPS)
+    assert np.array_equal(host(norm), np.zeros((rows, cols), np.float32))
+    assert np.array_equal(host(sm), np.zeros((rows, cols), np.float32))
+
+
+def test_residual_rmsnorm_null_weight_equals_unit_weight(pkg, dev):
+    """test_kernels.cu:1052-1085 (kAddRtol = kAddAtol = 0: bit-identical)."""
+    g = golden.load("residual_rmsnorm__32x4096_now")
+    rows, cols = 32, 4096
+    x, r = dev_t(g["x"]), dev_t(g["residual"])
+    ones = dev_t(np.ones(cols, np.float32))
+    outs = []
+    for wp in (0, ones.data_ptr()):
+        norm = torch.empty(rows, cols, device=dev)
+        sm = torch.empty(rows, cols, device=dev)
+        pkg.cuda.residual_rmsnorm(x.data_ptr(), r.data_ptr(), wp, norm.data_ptr(), sm.data_ptr(),
+                                  rows, cols, EPS)
+        outs.append((host(norm), host(sm)))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+
+
 def test_rmsnorm_linear_multi_stream(pkg, dev):
     """test_kernels.cu:1197: M=32 and M=1 calls interleaved on two streams."""
     K = N = 512

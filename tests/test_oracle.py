@@ -58,6 +58,14 @@ def test_oracle_rmsnorm_matches_golden(stem):
     _close(oracle.rmsnorm(g["input"], g.get("weight"), EPS), g["expected"], 1e-5, 1e-6)
 
 
+@pytest.mark.parametrize("stem", golden.stems("residual_rmsnorm__"))
+def test_oracle_residual_rmsnorm_matches_golden(stem):
+    g = golden.load(stem)
+    norm, sm = oracle.residual_rmsnorm(g["x"], g["residual"], g.get("weight"), EPS)
+    _close(norm, g["expected"], 1e-5, 1e-6)  # kRmsRtol / kRmsAtol, test_kernels.cu:141-142
+    assert np.array_equal(sm, g["sum_out"])  # one float addition, exactly the reference's
+
+
 def test_golden_case_inventory():
     """Every hot-path case of the reference's generator is present."""
     assert len(golden.stems("matmul__")) == 5
@@ -65,6 +73,7 @@ def test_golden_case_inventory():
     assert len(golden.stems("gemv_fp16__")) == 4
     assert len(golden.stems("rmsnorm_linear__")) == 5
     assert len(golden.stems("rmsnorm__")) == 5
+    assert len(golden.stems("residual_rmsnorm__")) == 5
 
 
 # ------------------------------------------------------- vs the reference's own code
@@ -101,6 +110,29 @@ def test_oracle_rmsnorm_linear_bit_exact_vs_reference(with_w):
     out = np.empty((M, K), np.float32)
     oracle.ref_lib().ref_rmsnorm(_p(x), _p(w), _p(out), M, K, EPS)
     assert np.array_equal(oracle.rmsnorm(x, w, EPS), out)
+
+
+@needs_ref
+@pytest.mark.parametrize("with_w,with_res,with_sum", [(True, True, True), (False, True, True),
+                                                      (True, False, True), (True, True, False)])
+def test_oracle_residual_rmsnorm_bit_exact_vs_reference(with_w, with_res, with_sum):
+    """residual, weight and sum_out may each be null in the CPU reference."""
+    import ctypes
+    rows, cols = 9, 333
+    rng = np.random.default_rng(cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    res = rng.standard_normal((rows, cols)).astype(np.float32) if with_res else None
+    w = (rng.standard_normal(cols) * 0.1 + 1).astype(np.float32) if with_w else None
+    outs = []
+    for fn in (oracle.lib().orc_residual_rmsnorm, oracle.ref_lib().ref_residual_rmsnorm):
+        norm = np.full((rows, cols), np.nan, np.float32)
+        sm = np.full((rows, cols), np.nan, np.float32) if with_sum else None
+        fn(_p(x), _p(res), _p(w), _p(norm), _p(sm), ctypes.c_int64(rows), ctypes.c_int64(cols),
+           ctypes.c_float(EPS))
+        outs.append((norm, sm))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    if with_sum:
+        assert np.array_equal(outs[0][1], outs[1][1])
 
 
 @needs_ref
