@@ -193,6 +193,21 @@ def cpu_gemm_throughput(target_s: float, nthreads: int, n: int = 4096):
     return flops / t / 1e12, kind, rows, t
 
 
+def headline_config(world: int) -> dict:
+    """The workload both arms quote (the reference arm adds how it ran it)."""
+    return {"workload": "FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] (FP32 accumulate) "
+                        "+ decode GEMV W[4096,14336] x",
+            "M": 4096, "N": 4096, "K": 4096, "parallelism": f"replicas x{world}"}
+
+
+def cpu_single_thread(cpu_seconds: float) -> dict:
+    """The reference's own framing (one thread) beside the all-cores figure: the
+    same GEMM on a smaller row sample, about a quarter of the all-cores time."""
+    v, kind, rows, t = cpu_gemm_throughput(max(1.0, min(5.0, cpu_seconds / 4)), 1)
+    return {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": kind,
+            "sample": f"{rows} of 4096 output rows of the 4096^3 GEMM, {t:.1f} s"}
+
+
 # --------------------------------------------------------------- distributed
 
 def dist_setup(gpus: int):
@@ -248,16 +263,17 @@ def run_reference(args):
     flops = 2.0 * rows * n * n * args.steps
     value = flops / total / 1e12
     sample = (f"{rows} of 4096 output rows of the 4096^3 GEMM per step "
-              f"(engine::cpu::matmul, FP16 inputs widened to float)")
+              f"({'engine::cpu::matmul' if kind == 'reference' else 'oracle port'}, "
+              f"FP16 inputs widened to float)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (fp64 accumulate)", "data": "synthetic",
-        "config": {"workload": "FP16 GEMM 4096x4096x4096 (reference CPU oracle, row sample)",
-                   "M": n, "N": n, "K": n},
+        "config": dict(headline_config(world), implementation="the reference's CPU code, "
+                       "a row sample of the GEMM per step"),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nthreads, "kind": kind,
-                         "sample": sample},
+                         "sample": sample, "single_thread": cpu_single_thread(4.0)},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -287,10 +303,12 @@ def time_launches(torch, fn, sets, steps, warmup, stream):
     return per, t0.elapsed_time(t1)
 
 
-def time_graph(torch, fn, sets, steps, warmup):
+def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False):
     """Captures `steps` launches (rotating operand sets) in one CUDA graph and
-    times one replay with CUDA events on the replay stream; returns ms per launch.
-    Launch-bound kernels (~5-25 us) are timed without host enqueue gaps."""
+    times `reps` replays with CUDA events on the replay stream; returns the
+    median ms per launch, or with stats=True {"median", "q1", "q3"} over the
+    replays.  Launch-bound kernels (~5-25 us) are timed without host enqueue
+    gaps."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -303,16 +321,22 @@ def time_graph(torch, fn, sets, steps, warmup):
             fn(sets[i % len(sets)], side.cuda_stream)
     g.replay()
     torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
     s = torch.cuda.current_stream()
-    e0.record(s)
-    g.replay()
-    e1.record(s)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    per = []
+    for _ in range(max(reps, 1)):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        per.append(e0.elapsed_time(e1) / steps)
     del g
-    return ms
+    med = statistics.median(per)
+    if not stats:
+        return med
+    q = statistics.quantiles(per, n=4) if len(per) > 1 else [med, med, med]
+    return {"median": med, "q1": q[0], "q3": q[2]}
 
 
 def secondary_configs(torch, pkg, dev, g, world, args):
@@ -465,7 +489,8 @@ def run_headline(args):
                                               s[2].data_ptr(), Nv, Kv, st)
     gsteps = max(args.steps, 50)
     barrier(world)
-    gemv_kernel_ms = max_over_ranks(time_graph(torch, gemv, wsets, gsteps, max(args.warmup, 3)), world)
+    gst = time_graph(torch, gemv, wsets, gsteps, max(args.warmup, 3), reps=7, stats=True)
+    gemv_kernel_ms = max_over_ranks(gst["median"], world)
     gbytes = 2.0 * (Nv * Kv + Kv + Nv)
     gemv_gbs = gbytes / (gemv_kernel_ms * 1e-3) / 1e9
     gemv_job = world * gemv_gbs
@@ -512,7 +537,8 @@ def run_headline(args):
         cpu = {"value": v, "unit": "TFLOP/s", "cores": nth, "kind": kind,
                "sample": f"{rows} of 4096 output rows of the 4096^3 GEMM "
                          f"({'engine::cpu::matmul' if kind == 'reference' else 'oracle port'}, "
-                         f"FP16 inputs widened to float), {t:.1f} s"}
+                         f"FP16 inputs widened to float), {t:.1f} s",
+               "single_thread": cpu_single_thread(args.cpu_seconds)}
 
     traffic = traffic_for("gemm_tc_4096")
     line = {
@@ -520,19 +546,21 @@ def run_headline(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,1) FP16 operands (torch Philox), W ~ N(0,0.02)",
-        "config": {"workload": "FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] "
-                               "(tcgen05, FP32 accumulate) + decode GEMV W[4096,14336] x",
-                   "M": n, "N": n, "K": n, "parallelism": f"replicas x{world}",
-                   "l2": "rotating operand pools larger than the 126 MB L2 "
-                         "(4 x 96 MiB GEMM sets, 4 x 112 MiB GEMV weights)"},
+        "config": dict(headline_config(world),
+                       l2="rotating operand pools larger than the 126 MB L2 "
+                          "(4 x 96 MiB GEMM sets, 4 x 112 MiB GEMV weights)"),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": achieved / peak_t, "traffic": traffic,
                      "peak_kind": f"{pk_kind} bf16 dense burst",
                      "kernel": "gemm_tc2_kernel<256> 4096^3 (2-SM tcgen05, 256x256 tiles, stream-K tail)",
-                     "kernel_ms": gemm_kernel_ms},
+                     "kernel_ms": gemm_kernel_ms,
+                     "kernel_ms_median": statistics.median(per),
+                     "kernel_ms_iqr": (lambda q: [q[0], q[2]])(statistics.quantiles(per, n=4))
+                     if len(per) > 1 else None},
         "gemv": {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / pk["hbm_gbs"],
                  "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
                  "kernel_us": gemv_kernel_ms * 1e3, "job_gbs": gemv_job,
+                 "kernel_us_iqr": [gst["q1"] * 1e3, gst["q3"] * 1e3],
                  "bytes_per_launch": gbytes, "traffic": traffic_for("gemv_nk_4096x14336"),
                  "timing": "CUDA graph of back-to-back launches, 4 x 112 MiB rotating weights"},
         "other_configs": secondary,
