@@ -430,6 +430,26 @@ def secondary_configs(torch, pkg, dev, g, world, args):
     out["matmul_f32_4096"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
     del sets, fn_f32
     torch.cuda.empty_cache()
+    return with_fractions(out)
+
+
+# FP32 SIMT peak for the CUDA-core GEMMs: 148 SMs x 128 FMA/clk x 2 FLOP x 1.965 GHz
+# (nominal; the measured peaks cover only copy bandwidth and bf16 tensor GEMM).
+FP32_SIMT_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
+def with_fractions(out: dict) -> dict:
+    """Adds each line's roofline fraction: HBM lines against the measured copy
+    bandwidth, tensor lines against the measured bf16 dense burst peak, FP32
+    CUDA-core lines against the nominal FP32 SIMT peak."""
+    pk, kind = peaks()
+    for name, d in out.items():
+        if "gbs" in d:
+            d["frac"], d["peak_kind"] = d["gbs"] / pk["hbm_gbs"], f"{kind} HBM copy"
+        elif name.startswith("matmul_f32"):
+            d["frac"], d["peak_kind"] = d["tflops"] / FP32_SIMT_TFLOPS, "nominal FP32 SIMT"
+        elif "tflops" in d:
+            d["frac"], d["peak_kind"] = d["tflops"] / pk["bf16_tflops"], f"{kind} bf16 dense burst"
     return out
 
 

@@ -49,3 +49,21 @@ def test_warmup_is_at_least_three():
     assert r.returncode == 0, r.stderr[-2000:]
     d = json.loads([ln for ln in r.stdout.splitlines() if ln.strip().startswith("{")][0])
     assert d["warmup"] == 3
+
+
+def test_secondary_lines_carry_their_roofline_fraction():
+    """Every other_configs line gets frac and peak_kind: HBM lines against the
+    measured copy bandwidth, tensor lines against the bf16 burst peak, FP32
+    CUDA-core lines against the nominal SIMT peak."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    pk, kind = b.peaks()
+    out = b.with_fractions({"gemv_4096x4096": {"us": 7.0, "gbs": 4800.0},
+                            "prefill_s2048": {"us": 180.0, "tflops": 1320.0},
+                            "matmul_f32_512": {"us": 14.6, "tflops": 18.3}})
+    assert out["gemv_4096x4096"]["frac"] == 4800.0 / pk["hbm_gbs"]
+    assert out["prefill_s2048"]["frac"] == 1320.0 / pk["bf16_tflops"]
+    assert abs(out["matmul_f32_512"]["frac"] - 18.3 / 74.4) < 1e-3
+    assert all("peak_kind" in d for d in out.values())
