@@ -24,7 +24,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libengine_b200.so"
 
-__all__ = ["EngineError", "lib", "cuda", "ops", "LIB_PATH", "EXPORTS", "build"]
+__all__ = ["EngineError", "lib", "cuda", "ops", "gguf", "LIB_PATH", "EXPORTS", "build"]
 
 
 class EngineError(RuntimeError):
@@ -35,10 +35,18 @@ class EngineError(RuntimeError):
         self.code = code
 
 
+class GgufTensorInfo(ctypes.Structure):
+    """engine_gguf_tensor_t (include/engine_b200.h)."""
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int32), ("n_dims", ctypes.c_int32),
+                ("dims", ctypes.c_int64 * 4), ("offset", ctypes.c_uint64),
+                ("nbytes", ctypes.c_uint64), ("data", ctypes.c_void_p)]
+
+
 # name -> (argtypes) ; every entry returns int status
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _f = ctypes.c_float
+_P = ctypes.POINTER
 EXPORTS: dict[str, list] = {
     "engine_cuda_matmul_naive": [_p, _p, _p, _i64, _i64, _i64, _p],
     "engine_cuda_matmul_tiled": [_p, _p, _p, _i64, _i64, _i64, _p],
@@ -63,6 +71,19 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_quant_repack": [ctypes.c_int, _p, _p, _p, _i64, _i64, _p],
     "engine_cuda_gemv_q_nk": [ctypes.c_int, _p, _p, _p, _p, _p, _i64, _i64, _p],
     "engine_tp_comm_create": [ctypes.c_int, ctypes.c_int, _i64, ctypes.POINTER(ctypes.c_void_p)],
+    "engine_gguf_open": [ctypes.c_char_p, _P(ctypes.c_void_p)],
+    "engine_gguf_close": [_p],
+    "engine_gguf_version": [_p, _P(ctypes.c_int32), _P(ctypes.c_uint64)],
+    "engine_gguf_tensor_count": [_p, _P(ctypes.c_int64)],
+    "engine_gguf_tensor": [_p, _i64, _P(GgufTensorInfo)],
+    "engine_gguf_find_tensor": [_p, ctypes.c_char_p, _P(ctypes.c_int64)],
+    "engine_gguf_meta_count": [_p, _P(ctypes.c_int64)],
+    "engine_gguf_meta_entry": [_p, _i64, _P(ctypes.c_char_p), _P(ctypes.c_int32),
+                               _P(ctypes.c_int32), _P(ctypes.c_uint64)],
+    "engine_gguf_meta_int": [_p, ctypes.c_char_p, _P(ctypes.c_int64)],
+    "engine_gguf_meta_float": [_p, ctypes.c_char_p, _P(ctypes.c_double)],
+    "engine_gguf_meta_string": [_p, ctypes.c_char_p, _P(ctypes.c_void_p), _P(ctypes.c_uint64)],
+    "engine_gguf_load_tensor": [_p, _i64, _p, _p, _p, _p],
     "engine_tp_comm_handle": [_p, _p],
     "engine_tp_comm_open": [_p, _p],
     "engine_tp_comm_destroy": [_p],
@@ -119,4 +140,4 @@ def device_status(device: int = 0) -> int:
     return int(flags.value)
 
 
-from . import cuda, ops, tp  # noqa: E402  (after lib/_check are defined)
+from . import cuda, gguf, ops, tp  # noqa: E402  (after lib/_check are defined)

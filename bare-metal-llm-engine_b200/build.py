@@ -58,7 +58,7 @@ def _compile(src: Path, verbose: bool, extra: list[str]) -> Path:
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
     extra = list(extra or [])
     OBJ.mkdir(exist_ok=True)
-    srcs = sorted(CSRC.glob("*.cu"))
+    srcs = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))  # .cpp: host-only code
     hdr_t = _newest_header()
     todo = []
     for s in srcs:

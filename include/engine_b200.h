@@ -57,7 +57,9 @@ enum {
   ENGINE_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
   ENGINE_ERR_UNSUPPORTED = 3, /* shape / alignment outside what the kernels support */
   ENGINE_ERR_DEVICE = 4,      /* a kernel reported a device-side error (wait timeout) */
-  ENGINE_ERR_INTERNAL = 5
+  ENGINE_ERR_INTERNAL = 5,
+  ENGINE_ERR_FORMAT = 6,      /* a model file is malformed or truncated */
+  ENGINE_ERR_IO = 7           /* a model file could not be opened or mapped */
 };
 
 /* Version of this ABI (bumped on any signature change). */
@@ -289,6 +291,91 @@ ENGINE_B200_API int engine_tp_linear_allreduce_f16(engine_tp_comm_t* comm, const
                                                    const engine_half_t* residual, engine_half_t* Y,
                                                    int64_t M, int64_t N, int64_t K,
                                                    engine_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * GGUF model files, memory-mapped, feeding the projections.  The engine plans a
+ * GGUF-style mmap'd loader (README.md:247, Module 7; tensor.hpp:19-23: weight
+ * tensors aliasing one mapped region) but has none; this is that loader's
+ * read side, for the weights the projections above consume.
+ *
+ * A file is GGUF version 2 or 3: header, typed metadata, tensor table, then the
+ * tensor data at general.alignment (default 32).  Every read is bounds-checked:
+ * a malformed or truncated file returns ENGINE_ERR_FORMAT, never a fault.
+ * Tensor dims are in the file's order: dims[0] is the contiguous extent (K of a
+ * [N,K] weight), and block-quantised rows run along dims[0].
+ * ------------------------------------------------------------------------- */
+typedef struct engine_gguf engine_gguf_t;
+
+/* GGML tensor type codes the loader can place on the device. */
+#define ENGINE_GGML_F32 0
+#define ENGINE_GGML_F16 1
+#define ENGINE_GGML_Q4_0 2
+#define ENGINE_GGML_Q8_0 8
+#define ENGINE_GGML_BF16 30
+
+/* GGUF metadata value type codes. */
+#define ENGINE_GGUF_UINT8 0
+#define ENGINE_GGUF_INT8 1
+#define ENGINE_GGUF_UINT16 2
+#define ENGINE_GGUF_INT16 3
+#define ENGINE_GGUF_UINT32 4
+#define ENGINE_GGUF_INT32 5
+#define ENGINE_GGUF_FLOAT32 6
+#define ENGINE_GGUF_BOOL 7
+#define ENGINE_GGUF_STRING 8
+#define ENGINE_GGUF_ARRAY 9
+#define ENGINE_GGUF_UINT64 10
+#define ENGINE_GGUF_INT64 11
+#define ENGINE_GGUF_FLOAT64 12
+
+typedef struct {
+  const char* name;   /* NUL-terminated, owned by the handle */
+  int32_t type;       /* GGML type code */
+  int32_t n_dims;     /* 1..4 */
+  int64_t dims[4];    /* dims[0] innermost; unused entries are 1 */
+  uint64_t offset;    /* absolute byte offset of the data in the file */
+  uint64_t nbytes;    /* 0 when the type's block size is unknown to the loader */
+  const void* data;   /* host pointer into the read-only mapping */
+} engine_gguf_tensor_t;
+
+/* Maps `path` read-only and parses it.  On success *out owns the mapping. */
+ENGINE_B200_API int engine_gguf_open(const char* path, engine_gguf_t** out);
+/* Unmaps and frees; null is a no-op. */
+ENGINE_B200_API int engine_gguf_close(engine_gguf_t* g);
+ENGINE_B200_API int engine_gguf_version(const engine_gguf_t* g, int32_t* version,
+                                        uint64_t* alignment);
+
+ENGINE_B200_API int engine_gguf_tensor_count(const engine_gguf_t* g, int64_t* n);
+ENGINE_B200_API int engine_gguf_tensor(const engine_gguf_t* g, int64_t index,
+                                       engine_gguf_tensor_t* out);
+/* ENGINE_ERR_INVALID when no tensor has that name. */
+ENGINE_B200_API int engine_gguf_find_tensor(const engine_gguf_t* g, const char* name,
+                                            int64_t* index);
+
+ENGINE_B200_API int engine_gguf_meta_count(const engine_gguf_t* g, int64_t* n);
+/* Key and value type of entry `index`; for arrays also the element type and count. */
+ENGINE_B200_API int engine_gguf_meta_entry(const engine_gguf_t* g, int64_t index,
+                                           const char** key, int32_t* type, int32_t* elem_type,
+                                           uint64_t* count);
+/* Typed lookups by key: ENGINE_ERR_INVALID when the key is missing or its value
+ * has another kind (integer types and bool read as int; float32/64 as float). */
+ENGINE_B200_API int engine_gguf_meta_int(const engine_gguf_t* g, const char* key, int64_t* v);
+ENGINE_B200_API int engine_gguf_meta_float(const engine_gguf_t* g, const char* key, double* v);
+ENGINE_B200_API int engine_gguf_meta_string(const engine_gguf_t* g, const char* key,
+                                            const char** s, uint64_t* len);
+
+/* Places tensor `index` on the device in the layout the projections read:
+ *  F32 / F16 / BF16: `payload` receives the nbytes of elements, row-major with
+ *    dims[0] contiguous (a [N,K] weight for linear_* / gemv_f16_nk);
+ *  Q8_0 / Q4_0: the packed blocks are copied to `staging` (device, >= nbytes)
+ *    and engine_cuda_quant_repack writes `payload` and `scales` for
+ *    engine_cuda_gemv_q_nk, with K = dims[0] and N = the product of the others.
+ * The host copy goes through pinned double buffers owned by the handle; the
+ * call returns once the copy and the repack are enqueued on `stream`, and the
+ * mapping must stay open until they finish.  Other types: ENGINE_ERR_UNSUPPORTED. */
+ENGINE_B200_API int engine_gguf_load_tensor(engine_gguf_t* g, int64_t index, void* payload,
+                                            engine_half_t* scales, void* staging,
+                                            engine_stream_t stream);
 
 #ifdef __cplusplus
 }
