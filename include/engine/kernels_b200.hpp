@@ -236,3 +236,10 @@ class TpComm {
 };
 
 }  // namespace engine::cuda
+
+// Tensor-typed overloads of the launchers above, when the engine's Tensor is on
+// the include path.
+#if __has_include(<engine/tensor.hpp>) && __has_include(<engine/config.hpp>)
+#include "kernels_b200_tensor.hpp"
+#endif
+
