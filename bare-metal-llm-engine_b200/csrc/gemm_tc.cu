@@ -1249,6 +1249,9 @@ int gemm_tc_general(const void* A, const void* B, const void* residual, void* C,
 int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C, int64_t M,
                     int64_t N, int64_t K, bool bf16, bool b_kmajor, bool hilo, int half_b,
                     cudaStream_t stream) {
+  // TMA tile coordinates and tile counts are 32-bit.
+  B200_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31),
+               "matmul: dimension too large (each must be below 2^31)");
   const CUtensorMapDataType dt =
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const uintptr_t pa = reinterpret_cast<uintptr_t>(A), pb = reinterpret_cast<uintptr_t>(B);

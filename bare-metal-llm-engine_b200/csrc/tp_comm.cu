@@ -340,15 +340,19 @@ int engine_tp_comm_create(int rank, int world, int64_t max_elems, engine_tp_comm
   B200_REQUIRE(world >= 1 && world <= kTpMaxWorld, "tp_comm_create: world must be in [1, 8]");
   B200_REQUIRE(rank >= 0 && rank < world, "tp_comm_create: rank must be in [0, world)");
   B200_REQUIRE(max_elems > 0, "tp_comm_create: max_elems must be positive");
+  // 2 parities x world x cap 8-byte words: bounded so the region size cannot overflow.
+  B200_REQUIRE(max_elems <= (int64_t(1) << 28), "tp_comm_create: max_elems must be at most 2^28");
   if (!kernels_fit())
     return set_error(ENGINE_ERR_UNSUPPORTED,
                      "tp_comm_create: the communicator kernels cannot keep 256 CTAs co-resident");
+  int device = 0;
+  B200_CUDA(cudaGetDevice(&device));
   auto* c = new (std::nothrow) engine_tp_comm();
   if (c == nullptr) return set_error(ENGINE_ERR_INTERNAL, "tp_comm_create: out of host memory");
   c->rank = rank;
   c->world = world;
   c->cap = (max_elems + 31) / 32 * 32;
-  B200_CUDA(cudaGetDevice(&c->device));
+  c->device = device;
   c->recv_bytes = align256(static_cast<size_t>(2) * world * c->cap * sizeof(unsigned long long));
   c->epoch_off = c->recv_bytes;
   c->region_bytes = c->epoch_off + align256(static_cast<size_t>(kTpCtas) * 4);
@@ -452,7 +456,8 @@ int engine_tp_linear_allreduce_f16(engine_tp_comm_t* comm, const engine_half_t* 
   B200_REQUIRE(M >= 0 && N >= 0 && K >= 0, "tp_linear_allreduce_f16: negative dimension");
   B200_REQUIRE(X != nullptr && W != nullptr && Y != nullptr,
                "tp_linear_allreduce_f16: null device pointer");
-  B200_REQUIRE(M * N <= comm->cap, "tp_linear_allreduce_f16: M*N exceeds the communicator's max_elems");
+  B200_REQUIRE(N == 0 || M <= comm->cap / N,
+               "tp_linear_allreduce_f16: M*N exceeds the communicator's max_elems");
   auto st = static_cast<cudaStream_t>(stream);
   const auto* x = reinterpret_cast<const __half*>(X);
   const auto* w = reinterpret_cast<const __half*>(W);

@@ -80,6 +80,9 @@ def test_launchers_reject_negative_dimensions(pkg):
     _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, -1, 4, 1e-5, substr="negative")
     _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, -1, 4, 1e-5, substr="negative")
     _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, 4, -1, 1e-5, substr="negative")
+    # tcgen05 tile coordinates are 32-bit: larger dimensions are rejected, not wrapped
+    _throws(pkg, c.matmul_f16, P, P, P, 2 ** 31, 8, 8, substr="too large")
+    _throws(pkg, c.matmul_f16, P, P, P, 8, 2 ** 31, 8, substr="too large")
     # eps < 0 would put a negative number under the square root.
     _throws(pkg, c.rmsnorm, P, P, P, 4, 4, -1.0, substr="eps")
     _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, 4, 4, -1.0, substr="eps")
@@ -180,6 +183,7 @@ def test_tp_comm_rejects_bad_arguments(pkg):
     _throws(pkg, c.tp_comm_create, 2, 2, 16, substr="rank")
     _throws(pkg, c.tp_comm_create, -1, 2, 16, substr="rank")
     _throws(pkg, c.tp_comm_create, 0, 2, 0, substr="max_elems")
+    _throws(pkg, c.tp_comm_create, 0, 2, 2 ** 40, substr="max_elems")
     _throws(pkg, c.tp_allreduce_f16, 0, P, 0, P, 8, substr="null")
     _throws(pkg, c.tp_linear_allreduce_f16, 0, P, P, 0, P, 1, 8, 8, substr="null")
     with pytest.raises(pkg.EngineError):
