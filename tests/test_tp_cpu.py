@@ -129,3 +129,77 @@ def test_weight_and_flop_accounting():
     cfg = tp.LLAMA3_8B
     assert abs(tp.weight_bytes_per_rank(cfg, 1) - 15.01e9) / 15.01e9 < 0.01
     assert tp.weight_bytes_per_rank(cfg, 8) * 8 == pytest.approx(tp.weight_bytes_per_rank(cfg, 1))
+
+
+# ------------------------------------------------------------ failure paths
+# A rank fails on the host, never on a GPU: it never joins, exits right after
+# joining, or raises before its first collective.  Rank 0 runs the TP layer
+# set; its rendezvous or its next all-reduce must end with an error within the
+# process group's short timeout, never hang.
+
+PG_TIMEOUT_S = 5
+
+
+def _fail_worker(rank, world, port, q, mode):
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    t0 = time.monotonic()
+    if mode == "never_joins" and rank == 1:
+        q.put((rank, "absent", 0.0))
+        return
+    joined = False
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=PG_TIMEOUT_S))
+        joined = True
+        if rank == 1 and mode == "exits_early":
+            q.put((rank, "exited", time.monotonic() - t0))
+            q.close()
+            q.join_thread()  # the message is flushed before the process vanishes
+            os._exit(0)  # leaves without a goodbye: its sockets close under rank 0
+        if rank == 1 and mode == "raises":
+            raise RuntimeError("failure injected on rank 1")
+        pkg = load_package()
+        from tests.tp_cpu_ops import CpuOps
+
+        tp = pkg.tp
+        run_model(tp, tp.TPConfig(**CFG_KW), world, rank, CpuOps())
+        q.put((rank, "ok", time.monotonic() - t0))
+    except Exception as e:  # the error is the expected outcome on rank 0
+        q.put((rank, "error: " + repr(e)[:300], time.monotonic() - t0))
+    finally:
+        if joined:
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+
+
+@pytest.mark.parametrize("mode", ["never_joins", "exits_early", "raises"])
+def test_tp_peer_failure_is_an_error_not_a_hang(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fail_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict((r, (s, t)) for r, s, t in (q.get(timeout=120) for _ in range(world)))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():  # never expected; do not leave a process behind
+                p.kill()
+                p.join()
+    status0, t0 = res[0]
+    assert status0.startswith("error"), f"rank 0 did not report the failed peer: {status0}"
+    # within the process-group timeout plus start-up (spawn, imports, the store)
+    assert t0 < PG_TIMEOUT_S + 60, f"rank 0 took {t0:.0f} s to notice"
+    assert res[1][0] in ({"never_joins": "absent", "exits_early": "exited"}.get(mode) or
+                         "error: RuntimeError('failure injected on rank 1')",)
