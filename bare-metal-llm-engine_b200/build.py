@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import json
 import os
 import shutil
 import subprocess
@@ -79,7 +80,30 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, OUT)
+        write_build_info()
     return OUT
+
+
+def write_build_info() -> None:
+    """Records what the library was built from beside it (build_info.json): the
+    git commit of the working tree, whether it had local changes, the nvcc
+    version and the compile flags.  The GPU box receives a snapshot without
+    .git, so the bench reads this file for its provenance block."""
+    def run(*cmd):
+        try:
+            return subprocess.run(cmd, capture_output=True, text=True, cwd=HERE, timeout=30).stdout.strip()
+        except Exception:
+            return ""
+    info = {
+        "git_commit": run("git", "rev-parse", "HEAD") or "unknown",
+        "git_dirty": bool(run("git", "status", "--porcelain", "--untracked-files=no")),
+        "nvcc": (run(nvcc(), "--version").splitlines() or ["unknown"])[-1],
+        "arch": ARCH[-1],
+        "flags": " ".join(FLAGS),
+        "built_utc": __import__("datetime").datetime.now(__import__("datetime").timezone.utc)
+        .strftime("%Y-%m-%dT%H:%M:%SZ"),
+    }
+    (HERE / "build_info.json").write_text(json.dumps(info, indent=1) + "\n")
 
 
 def main() -> int:

@@ -193,6 +193,38 @@ def cpu_gemm_throughput(target_s: float, nthreads: int, n: int = 4096):
     return flops / t / 1e12, kind, rows, t
 
 
+def environment(with_gpu: bool) -> dict:
+    """Provenance of a bench line: the library build (build_info.json, written by
+    build.py), the host, and with_gpu the device and driver."""
+    import platform
+
+    env = {"python": platform.python_version(), "host_cores": os.cpu_count()}
+    try:
+        with open("/proc/cpuinfo") as f:
+            env["host_cpu"] = next((ln.split(":", 1)[1].strip() for ln in f
+                                    if ln.startswith("model name")), platform.processor())
+    except OSError:
+        env["host_cpu"] = platform.processor()
+    bi = PKG_DIR / "build_info.json"
+    env["build"] = json.loads(bi.read_text()) if bi.exists() else None
+    if with_gpu:
+        import torch
+
+        p = torch.cuda.get_device_properties(torch.cuda.current_device())
+        env.update(device=p.name, sm_count=p.multi_processor_count,
+                   compute_capability=f"{p.major}.{p.minor}",
+                   memory_gib=round(p.total_memory / 2 ** 30, 1), torch=torch.__version__)
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            v = pynvml.nvmlSystemGetDriverVersion()
+            env["driver"] = v.decode() if isinstance(v, bytes) else v
+        except Exception:
+            env["driver"] = None
+    return env
+
+
 def headline_config(world: int) -> dict:
     """The workload both arms quote (the reference arm adds how it ran it)."""
     return {"workload": "FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] (FP32 accumulate) "
@@ -276,6 +308,7 @@ def run_reference(args):
                          "sample": sample, "single_thread": cpu_single_thread(4.0)},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "environment": environment(with_gpu=False),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -589,6 +622,7 @@ def run_headline(args):
         "cpu_baseline": cpu,
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
+        "environment": environment(with_gpu=True),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

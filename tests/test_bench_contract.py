@@ -39,6 +39,8 @@ def test_reference_arm_prints_one_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    env = d["environment"]  # provenance: host, and the library build when it exists
+    assert env["host_cores"] >= 1 and "python" in env
 
 
 def test_warmup_is_at_least_three():
