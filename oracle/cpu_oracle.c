@@ -334,6 +334,86 @@ void orc_swiglu_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int
   }
 }
 
+/* Causal / non-causal MHA / GQA attention, the two-pass FP64 oracle of
+ * src/cpu_ref/attention_cpu.cpp:87-155 (contract checks :27-66).
+ * Layouts: q / out [s_q][n_heads][head_dim]; k / v [n_kv_heads][s_kv][head_dim]
+ * with kv_head_stride elements between consecutive KV heads.  Query row i sees
+ * keys j <= q_pos_offset + i when causal (all keys otherwise); its scores are
+ * FP64 dot products of the widened halves times scale, the softmax is shifted
+ * by the row max, exponentials and the P.V accumulation are FP64, and the
+ * output is (acc / sum) rounded to float, then to half; lse = float(m +
+ * log(sum)).  A row with no visible key is zero with lse = -inf; s_kv == 0
+ * zeroes every row.  Returns 0, or 1 when an argument breaks the contract (the
+ * reference throws there). */
+int orc_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                  int64_t s_q, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads,
+                  int64_t head_dim, int64_t kv_head_stride, float scale, int64_t q_pos_offset,
+                  int is_causal, float* out_lse) {
+  if (!q || !k || !v || !out) return 1;
+  if (s_q < 0 || s_kv < 0 || q_pos_offset < 0 || n_heads <= 0 || n_kv_heads <= 0) return 1;
+  if (n_heads % n_kv_heads != 0 || (head_dim != 64 && head_dim != 128) || !isfinite(scale))
+    return 1;
+  if (kv_head_stride < (s_kv > 0 ? s_kv * head_dim : 0)) return 1;
+  if (s_q == 0) return 0;
+  const uint16_t zero = orc_f32_to_f16(0.0f);
+  if (s_kv == 0) {
+    for (int64_t i = 0; i < s_q * n_heads * head_dim; ++i) out[i] = zero;
+    if (out_lse)
+      for (int64_t i = 0; i < s_q * n_heads; ++i) out_lse[i] = -INFINITY;
+    return 0;
+  }
+  const int64_t group = n_heads / n_kv_heads;
+  const double scale_d = (double)scale;
+  double* scores = (double*)malloc((size_t)s_kv * sizeof(double));
+  double* acc = (double*)malloc((size_t)head_dim * sizeof(double));
+  if (!scores || !acc) {
+    free(scores);
+    free(acc);
+    return 1;
+  }
+  for (int64_t i = 0; i < s_q; ++i) {
+    int64_t max_j = s_kv - 1;
+    if (is_causal && q_pos_offset + i < max_j) max_j = q_pos_offset + i;
+    for (int64_t h = 0; h < n_heads; ++h) {
+      const int64_t row = i * n_heads + h;
+      const uint16_t* qr = q + row * head_dim;
+      uint16_t* orow = out + row * head_dim;
+      const uint16_t* kh = k + (h / group) * kv_head_stride;
+      const uint16_t* vh = v + (h / group) * kv_head_stride;
+      double m = -INFINITY;
+      for (int64_t j = 0; j <= max_j; ++j) {
+        double dot = 0.0;
+        for (int64_t d = 0; d < head_dim; ++d)
+          dot += (double)orc_f16_to_f32(qr[d]) * (double)orc_f16_to_f32(kh[j * head_dim + d]);
+        const double sc = dot * scale_d;
+        scores[j] = sc;
+        if (sc > m) m = sc;
+      }
+      double sum = 0.0;
+      if (max_j >= 0 && !(isinf(m) && m < 0.0)) {
+        for (int64_t d = 0; d < head_dim; ++d) acc[d] = 0.0;
+        for (int64_t j = 0; j <= max_j; ++j) {
+          const double w = exp(scores[j] - m);
+          sum += w;
+          for (int64_t d = 0; d < head_dim; ++d)
+            acc[d] += w * (double)orc_f16_to_f32(vh[j * head_dim + d]);
+        }
+      }
+      if (sum == 0.0) {  /* no visible key, or all scores -inf */
+        for (int64_t d = 0; d < head_dim; ++d) orow[d] = zero;
+        if (out_lse) out_lse[row] = -INFINITY;
+        continue;
+      }
+      const double inv = 1.0 / sum;
+      for (int64_t d = 0; d < head_dim; ++d) orow[d] = orc_f32_to_f16((float)(acc[d] * inv));
+      if (out_lse) out_lse[row] = (float)(m + log(sum));
+    }
+  }
+  free(scores);
+  free(acc);
+  return 0;
+}
+
 /* ------------------------------------------------- all-cores (row-split) forms */
 
 typedef struct {

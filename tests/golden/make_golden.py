@@ -7,7 +7,8 @@ The reference engine writes its golden data with ``tools/gen_reference.py``
 This script imports that generator read-only, runs it with its NumPy backend
 and, for every case on the matrix-multiply hot path (``matmul__*``,
 ``gemv__*``, ``gemv_fp16__*``, ``rmsnorm_linear__*``, the ``rmsnorm__*``
-dependency and the ``residual_rmsnorm__*`` epilogue), records:
+dependency, the ``residual_rmsnorm__*`` epilogue and the ``attention__*``
+cases of the next row), records:
 
 * the generator state immediately BEFORE the case's draws, so the inputs can be
   regenerated bit-for-bit anywhere NumPy is present (``golden.py`` replays the
@@ -33,7 +34,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 PREFIXES = ("matmul__", "gemv__", "gemv_fp16__", "rmsnorm_linear__", "rmsnorm__",
-            "residual_rmsnorm__")
+            "residual_rmsnorm__", "attention__")
+# Outputs stored verbatim (the rest of a case's tensors are inputs, replayed).
+OUTPUTS = ("expected", "lse")
 
 
 def sha(a: np.ndarray) -> str:
@@ -55,17 +58,26 @@ def main() -> int:
     state_before = rng.bit_generator.state
     cases = []
     expected = {}
+    attention = {c[0]: c[1:] for c in gen.ATTENTION_CASES}
     for stem, tensors in gen.build_cases(rng, backend):
         if stem.startswith(PREFIXES):
-            inputs = {k: sha(v) for k, v in tensors.items() if k != "expected"}
+            inputs = {k: sha(v) for k, v in tensors.items() if k not in OUTPUTS}
             shapes = {k: list(np.asarray(v).shape) for k, v in tensors.items()}
-            cases.append({
+            case = {
                 "stem": stem,
                 "state": state_before,
                 "input_sha256": inputs,
                 "shapes": shapes,
-            })
+            }
+            if stem.startswith("attention__"):  # the draws need the case's parameters
+                s_q, s_kv, h, h_kv, d, off, causal, amp = attention[stem[len("attention__"):]]
+                case["params"] = {"s_q": s_q, "s_kv": s_kv, "n_heads": h, "n_kv_heads": h_kv,
+                                  "head_dim": d, "q_pos_offset": off, "is_causal": bool(causal),
+                                  "qk_amp": float(amp)}
+            cases.append(case)
             expected[stem] = np.asarray(tensors["expected"]).astype(np.float32)
+            if "lse" in tensors:
+                expected[stem + "::lse"] = np.asarray(tensors["lse"]).astype(np.float32)
         state_before = rng.bit_generator.state
 
     meta = {

@@ -66,6 +66,25 @@ def test_oracle_residual_rmsnorm_matches_golden(stem):
     assert np.array_equal(sm, g["sum_out"])  # one float addition, exactly the reference's
 
 
+def _attention_tol(s_kv):
+    """test_kernels.cu:288-299 / test_cpu_ref.cpp:165-175: 2*eps16 relative and
+    1.5*eps16 + 4*s_kv*u32 absolute on the output; 2e-5 (+ 4*s_kv*u32) on lse."""
+    e16, u32 = 2.0 ** -10, 2.0 ** -23
+    return (2 * e16, 1.5 * e16 + 4 * s_kv * u32), (2e-5, 2e-5 + 4 * s_kv * u32)
+
+
+@pytest.mark.parametrize("stem", golden.stems("attention__"))
+def test_oracle_attention_matches_golden(stem):
+    g = golden.load(stem)
+    s_kv, d = g["k"].shape[1], g["q"].shape[2]
+    p = next(c for c in golden._meta()["cases"] if c["stem"] == stem)["params"]
+    out, lse = oracle.attention(g["q"], g["k"], g["v"], 1.0 / np.float32(np.sqrt(np.float32(d))),
+                                p["q_pos_offset"], p["is_causal"])
+    (rt, at), (lrt, lat) = _attention_tol(s_kv)
+    _close(out.astype(np.float32), g["expected"], rt, at)
+    _close(lse, g["lse"], lrt, lat)
+
+
 def test_golden_case_inventory():
     """Every hot-path case of the reference's generator is present."""
     assert len(golden.stems("matmul__")) == 5
@@ -74,6 +93,7 @@ def test_golden_case_inventory():
     assert len(golden.stems("rmsnorm_linear__")) == 5
     assert len(golden.stems("rmsnorm__")) == 5
     assert len(golden.stems("residual_rmsnorm__")) == 5
+    assert len(golden.stems("attention__")) == 10
 
 
 # ------------------------------------------------------- vs the reference's own code
@@ -133,6 +153,38 @@ def test_oracle_residual_rmsnorm_bit_exact_vs_reference(with_w, with_res, with_s
     assert np.array_equal(outs[0][0], outs[1][0])
     if with_sum:
         assert np.array_equal(outs[0][1], outs[1][1])
+
+
+@needs_ref
+@pytest.mark.parametrize("s_q,s_kv,h,h_kv,d,off,causal,amp", [
+    (1, 1, 1, 1, 64, 0, True, 1.0), (17, 17, 8, 2, 64, 0, True, 1.0),
+    (33, 65, 8, 2, 128, 32, True, 1.0), (1, 257, 32, 4, 64, 256, False, 1.0),
+    (16, 32, 4, 4, 64, 0, True, 4.0), (7, 300, 4, 1, 128, 100, True, 8.0),
+    (4, 0, 2, 1, 64, 0, True, 1.0)])
+def test_oracle_attention_bit_exact_vs_reference(s_q, s_kv, h, h_kv, d, off, causal, amp):
+    """src/cpu_ref/attention_cpu.cpp compiled in place: outputs and lse bit for
+    bit, GQA, causal offsets, decode shapes and s_kv = 0 included."""
+    rng = np.random.default_rng(s_q * 1000 + s_kv)
+    q = (rng.standard_normal((s_q, h, d)) * amp).astype(np.float16)
+    k = (rng.standard_normal((h_kv, s_kv, d)) * amp).astype(np.float16)
+    v = rng.standard_normal((h_kv, s_kv, d)).astype(np.float16)
+    scale = 1.0 / np.sqrt(d)
+    a = oracle.attention(q, k, v, scale, off, causal)
+    b = oracle.attention(q, k, v, scale, off, causal, ref=True)
+    assert np.array_equal(a[0].view(np.uint16), b[0].view(np.uint16))
+    assert np.array_equal(a[1], b[1])
+
+
+@needs_ref
+def test_oracle_attention_contract_matches_reference():
+    q = np.zeros((2, 4, 96), np.float16)  # head_dim 96 is outside the contract
+    k = np.zeros((2, 3, 96), np.float16)
+    for ref in (False, True):
+        with pytest.raises(ValueError):
+            oracle.attention(q, k, k, 0.1, 0, True, ref=ref)
+        with pytest.raises(ValueError):  # 3 heads over 2 KV heads
+            oracle.attention(np.zeros((2, 3, 64), np.float16), np.zeros((2, 3, 64), np.float16),
+                             np.zeros((2, 3, 64), np.float16), 0.1, 0, True, ref=ref)
 
 
 @needs_ref
