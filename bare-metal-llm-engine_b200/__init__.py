@@ -71,6 +71,10 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_quant_repack": [ctypes.c_int, _p, _p, _p, _i64, _i64, _p],
     "engine_cuda_gemv_q_nk": [ctypes.c_int, _p, _p, _p, _p, _p, _i64, _i64, _p],
     "engine_tp_comm_create": [ctypes.c_int, ctypes.c_int, _i64, ctypes.POINTER(ctypes.c_void_p)],
+    "engine_cuda_attention_prefill": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i64,
+                                      ctypes.c_int, _p, _p],
+    "engine_cuda_attention_decode": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f, ctypes.c_int,
+                                     _p],
     "engine_gguf_open": [ctypes.c_char_p, _P(ctypes.c_void_p)],
     "engine_gguf_close": [_p],
     "engine_gguf_version": [_p, _P(ctypes.c_int32), _P(ctypes.c_uint64)],

@@ -1,0 +1,366 @@
+// attention.cu -- MHA / GQA attention: split-KV decode and a prefill baseline.
+//
+// Layouts and contract of the engine's launchers (include/engine/kernels.hpp:153
+// attention_prefill, :191 attention_decode; kernels/attention_prefill.cu:329-360,
+// kernels/attention_decode.cu:637-660): q / out [s_q][n_heads][d], k / v
+// [n_kv_heads][kv_head_stride] with key j of a KV head at j * d, d = 64 or 128,
+// query head h reading KV head h / (n_heads / n_kv_heads).  Query row i sees
+// keys j <= q_pos_offset + i when causal, every key otherwise.
+//
+// One kernel serves both entry points.  A CTA takes one query position, up to
+// four query heads of one KV group and one split of the key range:
+// - Its 4 warps stream that KV head's K and V rows of the split with 16-byte
+//   loads (d / 8 lanes per key row), shared by the CTA's query heads, so K and V
+//   cross HBM once per split -- the decode bound.
+// - Each group of d / 8 lanes runs an FP32 online softmax over its keys: the
+//   running max m, sum l and the lane's 8 elements of the output accumulator.
+// - The CTA merges its lane groups in fixed order through shared memory; a
+//   single split writes out (and lse) directly, more splits write (m, l, O) to
+//   a workspace that attn_merge_kernel combines in split order.
+// Decode (one query position) gets enough splits to fill the GPU.  Prefill runs
+// the same kernel per query position: a correctness baseline for the engine's
+// prefill API; the tensor-core FlashAttention-2 prefill is the next step.
+#include <cmath>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace b200 {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnUnroll = 4;  // keys per lane group per step (loads issued first)
+
+template <bool VEC>
+__device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
+  if constexpr (VEC) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __half2float(p[i]);
+  }
+}
+
+struct AttnArgs {
+  const __half* q;
+  const __half* k;
+  const __half* v;
+  __half* out;
+  float* lse;
+  float* ws;  // [s_q * n_heads][splits][d + 2]: m, l, O[d]
+  int64_t s_q, s_kv, n_heads, n_kv_heads, kv_head_stride, q_pos_offset;
+  float scale;
+  int causal;
+  int splits;
+  int64_t chunk;  // keys per split
+};
+
+// grid: (splits, n_kv_heads * (group / GB), s_q); block: 128 threads.
+template <int D, int GB, bool VEC, bool FINAL>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnArgs a) {
+  constexpr int LPK = D / 8;               // lanes per key row
+  constexpr int KPW = 32 / LPK;            // key rows per warp
+  constexpr int NKG = kAttnWarps * KPW;    // lane groups per CTA
+  __shared__ float s_m[NKG][GB], s_l[NKG][GB];
+  __shared__ float s_o[NKG][GB][D];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane % LPK;              // this lane's 8 elements: [8 sub, 8 sub + 8)
+  const int kgw = lane / LPK;              // lane group within the warp
+  const int kg = warp * KPW + kgw;         // lane group within the CTA
+  const int64_t group = a.n_heads / a.n_kv_heads;
+  const int64_t chunks_per_kv = group / GB;
+  const int64_t h_kv = blockIdx.y / chunks_per_kv;
+  const int64_t h0 = h_kv * group + (blockIdx.y % chunks_per_kv) * GB;  // first query head
+  const int64_t i = blockIdx.z;                                         // query position
+  const int split = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
+
+  int64_t max_j = a.s_kv - 1;
+  if (a.causal && a.q_pos_offset + i < max_j) max_j = a.q_pos_offset + i;
+  const int64_t j0 = static_cast<int64_t>(split) * a.chunk;
+  int64_t j1 = j0 + a.chunk;
+  if (j1 > max_j + 1) j1 = max_j + 1;  // keys [j0, j1) of this split are visible
+
+  float qf[GB][8];
+#pragma unroll
+  for (int g = 0; g < GB; ++g) {
+    load8<VEC>(a.q + ((i * a.n_heads) + h0 + g) * D + 8 * sub, qf[g]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qf[g][e] *= a.scale;
+  }
+  float m[GB], l[GB], o[GB][8];
+#pragma unroll
+  for (int g = 0; g < GB; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[g][e] = 0.0f;
+  }
+  const __half* kh = a.k + h_kv * a.kv_head_stride + 8 * sub;
+  const __half* vh = a.v + h_kv * a.kv_head_stride + 8 * sub;
+  // The loop bound is uniform across the warp (the shuffles below need every
+  // lane); lane group kgw takes key jw + kgw + u * NKG.
+  for (int64_t jw = j0 + static_cast<int64_t>(warp) * KPW; jw < j1;
+       jw += static_cast<int64_t>(NKG) * kAttnUnroll) {
+    const int64_t jb = jw + kgw;
+    float kf[kAttnUnroll][8], vf[kAttnUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      const int64_t j = jb + static_cast<int64_t>(u) * NKG;
+      if (j < j1) {
+        load8<VEC>(kh + j * D, kf[u]);
+        load8<VEC>(vh + j * D, vf[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kAttnUnroll; ++u) {
+      const int64_t j = jb + static_cast<int64_t>(u) * NKG;
+      const bool valid = j < j1;  // uniform within a lane group
+#pragma unroll
+      for (int g = 0; g < GB; ++g) {
+        float s = 0.0f;
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s = fmaf(qf[g][e], kf[u][e], s);
+        }
+#pragma unroll
+        for (int off = LPK / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (valid) {
+          const float mn = fmaxf(m[g], s);
+          const float alpha = expf(m[g] - mn);  // m = -inf first: alpha = 0
+          const float p = expf(s - mn);
+          l[g] = l[g] * alpha + p;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[g][e] = fmaf(p, vf[u][e], o[g][e] * alpha);
+          m[g] = mn;
+        }
+      }
+    }
+  }
+  // merge the lane groups in fixed order
+#pragma unroll
+  for (int g = 0; g < GB; ++g) {
+    if (sub == 0) {
+      s_m[kg][g] = m[g];
+      s_l[kg][g] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_o[kg][g][8 * sub + e] = o[g][e];
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < GB * D; t += blockDim.x) {
+    const int g = t / D, d = t % D;
+    float M = -INFINITY;
+    for (int c = 0; c < NKG; ++c) M = fmaxf(M, s_m[c][g]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+      for (int c = 0; c < NKG; ++c) {
+        if (s_m[c][g] == -INFINITY) continue;
+        const float w = expf(s_m[c][g] - M);
+        L = fmaf(s_l[c][g], w, L);
+        O = fmaf(s_o[c][g][d], w, O);
+      }
+    }
+    const int64_t row = i * a.n_heads + h0 + g;
+    if constexpr (FINAL) {
+      a.out[row * D + d] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
+      if (d == 0 && a.lse != nullptr) a.lse[row] = L > 0.0f ? M + logf(L) : -INFINITY;
+    } else {
+      float* w = a.ws + (row * a.splits + split) * (D + 2);
+      if (d == 0) {
+        w[0] = M;
+        w[1] = L;
+      }
+      w[2 + d] = O;
+    }
+  }
+}
+
+// One thread per (row, element): the splits' (m, l, O) combined in split order.
+template <int D>
+__global__ void __launch_bounds__(256) attn_merge_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t rows = a.s_q * a.n_heads;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < rows * D;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = t / D;
+    const int d = static_cast<int>(t % D);
+    const float* w = a.ws + row * a.splits * (D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, w[s * (D + 2)]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < a.splits; ++s) {
+        const float ms = w[s * (D + 2)];
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - M);
+        L = fmaf(w[s * (D + 2) + 1], f, L);
+        O = fmaf(w[s * (D + 2) + 2 + d], f, O);
+      }
+    }
+    a.out[row * D + d] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
+    if (d == 0 && a.lse != nullptr) a.lse[row] = L > 0.0f ? M + logf(L) : -INFINITY;
+  }
+}
+
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[t] = v;
+}
+
+template <int D, int GB, bool VEC>
+int launch_split(AttnArgs& a, cudaStream_t st) {
+  const int64_t group = a.n_heads / a.n_kv_heads;
+  const dim3 grid(static_cast<unsigned>(a.splits),
+                  static_cast<unsigned>(a.n_kv_heads * (group / GB)), static_cast<unsigned>(a.s_q));
+  if (a.splits == 1) {
+    B200_CUDA(launch_pdl(attn_split_kernel<D, GB, VEC, true>, grid, dim3(kAttnWarps * 32), 0, st, a));
+  } else {
+    B200_CUDA(launch_pdl(attn_split_kernel<D, GB, VEC, false>, grid, dim3(kAttnWarps * 32), 0, st, a));
+    const int64_t total = a.s_q * a.n_heads * D;
+    const int64_t blocks64 = (total + 255) / 256;
+    const unsigned blocks = static_cast<unsigned>(blocks64 < 65535 ? blocks64 : 65535);
+    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(blocks), dim3(256), 0, st, a));
+  }
+  return ENGINE_OK;
+}
+
+template <int D, bool VEC>
+int launch_gb(AttnArgs& a, cudaStream_t st) {
+  const int64_t group = a.n_heads / a.n_kv_heads;
+  if (group % 4 == 0) return launch_split<D, 4, VEC>(a, st);
+  if (group % 2 == 0) return launch_split<D, 2, VEC>(a, st);
+  return launch_split<D, 1, VEC>(a, st);
+}
+
+// Shared body of both entry points (arguments already validated).
+int run_attention(const __half* q, const __half* k, const __half* v, __half* out, int64_t s_q,
+                  int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d, int64_t stride,
+                  float scale, int64_t q_pos_offset, bool causal, float* lse, int split_kv,
+                  cudaStream_t st, const char* what) {
+  if (s_q == 0) return ENGINE_OK;
+  if (s_kv == 0) {
+    B200_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(s_q * n_heads * d) * 2, st));
+    if (lse != nullptr) {
+      fill_kernel<<<static_cast<unsigned>((s_q * n_heads + 255) / 256), 256, 0, st>>>(
+          lse, s_q * n_heads, -INFINITY);
+    }
+    return check_launch(what);
+  }
+  AttnArgs a{q, k, v, out, lse, nullptr, s_q, s_kv, n_heads, n_kv_heads, stride, q_pos_offset,
+             scale, causal ? 1 : 0, 1, s_kv};
+  const int64_t group = n_heads / n_kv_heads;
+  const int64_t gb = group % 4 == 0 ? 4 : (group % 2 == 0 ? 2 : 1);
+  const int64_t ctas = s_q * n_kv_heads * (group / gb);
+  int64_t splits = split_kv;
+  if (splits <= 0) {  // enough CTAs for two per SM, each split at least 128 keys
+    const int64_t want = (2 * static_cast<int64_t>(sm_count()) + ctas - 1) / ctas;
+    const int64_t most = (s_kv + 127) / 128;
+    splits = want < most ? want : most;
+    if (splits < 1) splits = 1;
+  }
+  if (splits > s_kv) splits = s_kv;
+  if (splits > 65535) splits = 65535;
+  a.chunk = (s_kv + splits - 1) / splits;
+  a.splits = static_cast<int>((s_kv + a.chunk - 1) / a.chunk);
+  float* ws = nullptr;
+  if (a.splits > 1) {
+    const size_t bytes = static_cast<size_t>(s_q * n_heads) * a.splits * (d + 2) * sizeof(float);
+    ws = static_cast<float*>(scratch_alloc(bytes, st));
+    if (ws == nullptr) return set_error(ENGINE_ERR_CUDA, std::string(what) + ": workspace allocation failed");
+    a.ws = ws;
+  }
+  const bool vec = (reinterpret_cast<uintptr_t>(q) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(k) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(v) % 16 == 0) && (stride % 8 == 0);
+  int rc;
+  if (d == 64) {
+    rc = vec ? launch_gb<64, true>(a, st) : launch_gb<64, false>(a, st);
+  } else {
+    rc = vec ? launch_gb<128, true>(a, st) : launch_gb<128, false>(a, st);
+  }
+  if (ws != nullptr) scratch_free(ws, st);
+  if (rc != ENGINE_OK) return rc;
+  return check_launch(what);
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" {
+
+int engine_cuda_attention_prefill(const engine_half_t* q, const engine_half_t* k,
+                                  const engine_half_t* v, engine_half_t* out, int64_t s_q,
+                                  int64_t s_kv, int64_t n_heads, int64_t n_kv_heads,
+                                  int64_t head_dim, int64_t kv_head_stride, float scale,
+                                  int64_t q_pos_offset, int is_causal, float* out_lse,
+                                  engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(q != nullptr, "attention_prefill: q is null");
+  B200_REQUIRE(k != nullptr, "attention_prefill: k is null");
+  B200_REQUIRE(v != nullptr, "attention_prefill: v is null");
+  B200_REQUIRE(out != nullptr, "attention_prefill: out is null");
+  B200_REQUIRE(s_q >= 0, "attention_prefill: s_q must be non-negative");
+  B200_REQUIRE(s_kv >= 0, "attention_prefill: s_kv must be non-negative");
+  B200_REQUIRE(q_pos_offset >= 0, "attention_prefill: q_pos_offset must be non-negative");
+  B200_REQUIRE(n_heads > 0, "attention_prefill: n_heads must be positive");
+  B200_REQUIRE(n_kv_heads > 0, "attention_prefill: n_kv_heads must be positive");
+  B200_REQUIRE(n_heads % n_kv_heads == 0,
+               "attention_prefill: n_heads must be divisible by n_kv_heads");
+  B200_REQUIRE(head_dim == 64 || head_dim == 128,
+               "attention_prefill: head_dim must be 64 or 128");
+  B200_REQUIRE(std::isfinite(scale), "attention_prefill: scale must be finite");
+  B200_REQUIRE(kv_head_stride >= (s_kv > 0 ? s_kv * head_dim : 0),
+               "attention_prefill: kv_head_stride < s_kv * head_dim");
+  B200_REQUIRE(s_q <= 65535 && n_heads <= 65535, "attention_prefill: s_q or n_heads too large");
+  return run_attention(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
+                       reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(out), s_q,
+                       s_kv, n_heads, n_kv_heads, head_dim, kv_head_stride, scale, q_pos_offset,
+                       is_causal != 0, out_lse, 0, static_cast<cudaStream_t>(stream),
+                       "attention_prefill");
+  B200_ENTRY_END
+}
+
+int engine_cuda_attention_decode(const engine_half_t* q, const engine_half_t* k,
+                                 const engine_half_t* v, engine_half_t* out, int64_t kv_len,
+                                 int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                                 int64_t kv_head_stride, float scale, int split_kv,
+                                 engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(q != nullptr, "attention_decode: q is null");
+  B200_REQUIRE(k != nullptr, "attention_decode: k is null");
+  B200_REQUIRE(v != nullptr, "attention_decode: v is null");
+  B200_REQUIRE(out != nullptr, "attention_decode: out is null");
+  B200_REQUIRE(kv_len >= 0, "attention_decode: kv_len must be non-negative");
+  B200_REQUIRE(n_heads > 0, "attention_decode: n_heads must be positive");
+  B200_REQUIRE(n_kv_heads > 0, "attention_decode: n_kv_heads must be positive");
+  B200_REQUIRE(n_heads % n_kv_heads == 0,
+               "attention_decode: n_heads must be divisible by n_kv_heads");
+  B200_REQUIRE(head_dim == 64 || head_dim == 128,
+               "attention_decode: head_dim must be 64 or 128");
+  B200_REQUIRE(std::isfinite(scale), "attention_decode: scale must be finite");
+  B200_REQUIRE(split_kv >= 0, "attention_decode: split_kv must be non-negative");
+  B200_REQUIRE(kv_head_stride >= (kv_len > 0 ? kv_len * head_dim : 0),
+               "attention_decode: kv_head_stride < kv_len * head_dim");
+  B200_REQUIRE(n_heads <= 65535, "attention_decode: n_heads too large");
+  return run_attention(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
+                       reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(out), 1,
+                       kv_len, n_heads, n_kv_heads, head_dim, kv_head_stride, scale, 0, false,
+                       nullptr, split_kv, static_cast<cudaStream_t>(stream), "attention_decode");
+  B200_ENTRY_END
+}
+
+}  // extern "C"

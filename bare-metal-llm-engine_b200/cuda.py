@@ -44,6 +44,19 @@ def residual_rmsnorm(x, residual, weight, norm_out, sum_out, rows, cols, eps,  #
                                               eps, _s(stream)))
 
 
+def attention_prefill(q, k, v, out, s_q, s_kv, n_heads, n_kv_heads, head_dim,  # kernels.hpp:153
+                      kv_head_stride, scale, q_pos_offset=0, is_causal=True, out_lse=0, stream=0):
+    _check(lib().engine_cuda_attention_prefill(q, k, v, out, s_q, s_kv, n_heads, n_kv_heads,
+                                               head_dim, kv_head_stride, scale, q_pos_offset,
+                                               1 if is_causal else 0, out_lse, _s(stream)))
+
+
+def attention_decode(q, k, v, out, kv_len, n_heads, n_kv_heads, head_dim,  # kernels.hpp:191
+                     kv_head_stride, scale, split_kv=0, stream=0):
+    _check(lib().engine_cuda_attention_decode(q, k, v, out, kv_len, n_heads, n_kv_heads, head_dim,
+                                              kv_head_stride, scale, split_kv, _s(stream)))
+
+
 def rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, stream=0):  # kernels.hpp:97
     _check(lib().engine_cuda_rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, _s(stream)))
 

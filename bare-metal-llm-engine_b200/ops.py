@@ -154,6 +154,36 @@ def residual_rmsnorm(x, residual, weight=None, eps: float = 1e-5):
     return norm, sm
 
 
+def attention(q, k, v, scale=None, q_pos_offset: int = 0, is_causal: bool = True,
+              want_lse: bool = False):
+    """out [s_q, H, d] (FP16) of q [s_q, H, d] over k / v [H_kv, s_kv, d]
+    (engine::cuda::attention_prefill); with want_lse also lse [s_q, H] (FP32)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _req(t, torch.float16, n)
+    s_q, H, d = q.shape
+    H_kv, s_kv, _ = k.shape
+    scale = d ** -0.5 if scale is None else scale
+    out = torch.empty_like(q)
+    lse = torch.empty(s_q, H, device=q.device, dtype=torch.float32) if want_lse else None
+    _c.attention_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), s_q, s_kv, H,
+                         H_kv, d, s_kv * d, scale, q_pos_offset, is_causal, _ptr(lse), _stream())
+    return (out, lse) if want_lse else out
+
+
+def attention_decode(q, k, v, scale=None, split_kv: int = 0):
+    """out [H, d] of one query row q [H, d] over all kv_len keys of k / v
+    [H_kv, kv_len, d] (engine::cuda::attention_decode, split-KV)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _req(t, torch.float16, n)
+    H, d = q.shape
+    H_kv, kv_len, _ = k.shape
+    scale = d ** -0.5 if scale is None else scale
+    out = torch.empty_like(q)
+    _c.attention_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), kv_len, H, H_kv,
+                        d, kv_len * d, scale, split_kv, _stream())
+    return out
+
+
 def swiglu(gate, up, out=None):
     _req(gate, torch.float16, "gate")
     _req(up, torch.float16, "up")

@@ -194,6 +194,28 @@ inline void gemv_q_nk(int qtype, const void* payload, const __half* scales, cons
                                            b200_detail::h(y), N, K, stream));
 }
 
+// kernels.hpp:153 / :191 -- attention
+inline void attention_prefill(const __half* q, const __half* k, const __half* v, __half* out,
+                              std::int64_t s_q, std::int64_t s_kv, std::int64_t n_heads,
+                              std::int64_t n_kv_heads, std::int64_t head_dim,
+                              std::int64_t kv_head_stride, float scale,
+                              std::int64_t q_pos_offset = 0, bool is_causal = true,
+                              float* out_lse = nullptr, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_attention_prefill(
+      b200_detail::h(q), b200_detail::h(k), b200_detail::h(v), b200_detail::h(out), s_q, s_kv,
+      n_heads, n_kv_heads, head_dim, kv_head_stride, scale, q_pos_offset, is_causal ? 1 : 0,
+      out_lse, stream));
+}
+
+inline void attention_decode(const __half* q, const __half* k, const __half* v, __half* out,
+                             std::int64_t kv_len, std::int64_t n_heads, std::int64_t n_kv_heads,
+                             std::int64_t head_dim, std::int64_t kv_head_stride, float scale,
+                             int split_kv = 0, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_attention_decode(
+      b200_detail::h(q), b200_detail::h(k), b200_detail::h(v), b200_detail::h(out), kv_len,
+      n_heads, n_kv_heads, head_dim, kv_head_stride, scale, split_kv, stream));
+}
+
 // -- tensor-parallel communicator (engine_tp_*) --------------------------------
 // One per rank, on the rank's current device.  The host exchanges handle()
 // between the ranks (all-gather), then calls open() with all of them in rank

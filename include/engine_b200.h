@@ -293,6 +293,31 @@ ENGINE_B200_API int engine_tp_linear_allreduce_f16(engine_tp_comm_t* comm, const
                                                    engine_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Attention (MHA / GQA), the engine's launchers: q / out [s_q][n_heads][d],
+ * k / v [n_kv_heads][kv_head_stride], d = 64 or 128; query row i sees keys
+ * j <= q_pos_offset + i when causal.  Same contract and messages as
+ * kernels/attention_prefill.cu:329-360 and kernels/attention_decode.cu:637-660.
+ * ------------------------------------------------------------------------- */
+
+/* kernels.hpp:153 (attention_prefill).  out_lse [s_q][n_heads] may be null. */
+ENGINE_B200_API int engine_cuda_attention_prefill(const engine_half_t* q, const engine_half_t* k,
+                                                  const engine_half_t* v, engine_half_t* out,
+                                                  int64_t s_q, int64_t s_kv, int64_t n_heads,
+                                                  int64_t n_kv_heads, int64_t head_dim,
+                                                  int64_t kv_head_stride, float scale,
+                                                  int64_t q_pos_offset, int is_causal,
+                                                  float* out_lse, engine_stream_t stream);
+
+/* kernels.hpp:191 (attention_decode): one query row per head over kv_len keys,
+ * split-KV; split_kv = 0 chooses the split count. */
+ENGINE_B200_API int engine_cuda_attention_decode(const engine_half_t* q, const engine_half_t* k,
+                                                 const engine_half_t* v, engine_half_t* out,
+                                                 int64_t kv_len, int64_t n_heads,
+                                                 int64_t n_kv_heads, int64_t head_dim,
+                                                 int64_t kv_head_stride, float scale, int split_kv,
+                                                 engine_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * GGUF model files, memory-mapped, feeding the projections.  The engine plans a
  * GGUF-style mmap'd loader (README.md:247, Module 7; tensor.hpp:19-23: weight
  * tensors aliasing one mapped region) but has none; this is that loader's

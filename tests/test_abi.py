@@ -80,6 +80,20 @@ def test_launchers_reject_negative_dimensions(pkg):
     _throws(pkg, c.rmsnorm_linear_f16, P, P, P, 0, P, 4, -1, 4, 1e-5, substr="negative")
     _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, -1, 4, 1e-5, substr="negative")
     _throws(pkg, c.residual_rmsnorm, P, P, P, P, P, 4, -1, 1e-5, substr="negative")
+    # attention: the reference launchers' contracts (attention_prefill.cu:331-347,
+    # attention_decode.cu:637-652)
+    ap, ad = c.attention_prefill, c.attention_decode
+    _throws(pkg, ap, P, P, P, P, -1, 4, 2, 2, 64, 256, 0.1, substr="s_q must be non-negative")
+    _throws(pkg, ap, P, P, P, P, 4, 4, 3, 2, 64, 256, 0.1, substr="divisible")
+    _throws(pkg, ap, P, P, P, P, 4, 4, 2, 2, 96, 384, 0.1, substr="head_dim must be 64 or 128")
+    _throws(pkg, ap, P, P, P, P, 4, 4, 2, 2, 64, 100, 0.1, substr="kv_head_stride")
+    _throws(pkg, ap, P, P, P, P, 4, 4, 2, 2, 64, 256, float("inf"), substr="scale must be finite")
+    _throws(pkg, ap, P, P, P, P, 4, 4, 2, 2, 64, 256, 0.1, -1, substr="q_pos_offset")
+    _throws(pkg, ad, P, P, P, P, 4, 2, 2, 64, 256, 0.1, -1, substr="split_kv")
+    _throws(pkg, ad, P, P, P, P, -1, 2, 2, 64, 256, 0.1, substr="kv_len must be non-negative")
+    _throws(pkg, ad, 0, P, P, P, 4, 2, 2, 64, 256, 0.1, substr="q is null")
+    _throws(pkg, ap, P, P, P, 0, 4, 4, 2, 2, 64, 256, 0.1, substr="out is null")
+    c.attention_prefill(P, P, P, P, 0, 4, 2, 2, 64, 256, 0.1)  # s_q = 0: a no-op
     # tcgen05 tile coordinates are 32-bit: larger dimensions are rejected, not wrapped
     _throws(pkg, c.matmul_f16, P, P, P, 2 ** 31, 8, 8, substr="too large")
     _throws(pkg, c.matmul_f16, P, P, P, 8, 2 ** 31, 8, substr="too large")

@@ -1,0 +1,148 @@
+"""GPU: attention_prefill / attention_decode through the C ABI.
+
+Against the reference's golden attention cases (outputs and LSE) with its own
+derived tolerances (test_kernels.cu:288-299: 2*eps16 relative, 1.5*eps16 +
+4*s_kv*u32 absolute; LSE 2e-5 + 4*s_kv*u32), and against the oracle
+(orc_attention, pinned bit-exact to the reference's attention_cpu.cpp) at
+Llama-3-8B shapes: 32 query heads over 8 KV heads, d = 128, causal prefill
+with an offset, decode over 4096 keys for several split counts.  Edge cases:
+no keys (zeros, lse = -inf), a KV stride that is not a multiple of 8 (the
+scalar-load path), determinism.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from tests.golden import golden
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+E16, U32 = 2.0 ** -10, 2.0 ** -23
+
+
+def _tol(s_kv):
+    return (2 * E16, 1.5 * E16 + 4 * s_kv * U32), (2e-5, 2e-5 + 4 * s_kv * U32)
+
+
+def _close(got, want, rtol, atol, what):
+    np.testing.assert_allclose(np.asarray(got, np.float64), np.asarray(want, np.float64),
+                               rtol=rtol, atol=atol, err_msg=what)
+
+
+def _scale(d):
+    return float(np.float32(1.0) / np.sqrt(np.float32(d)))
+
+
+@pytest.mark.parametrize("stem", golden.stems("attention__"))
+def test_prefill_matches_golden(pkg, dev, stem):
+    g = golden.load(stem)
+    p = next(c for c in golden._meta()["cases"] if c["stem"] == stem)["params"]
+    q, k, v = (torch.from_numpy(g[n]).to(dev) for n in ("q", "k", "v"))
+    out, lse = pkg.ops.attention(q, k, v, _scale(p["head_dim"]), p["q_pos_offset"],
+                                 p["is_causal"], want_lse=True)
+    (rt, at), (lrt, lat) = _tol(p["s_kv"])
+    _close(out.cpu().numpy().astype(np.float32), g["expected"], rt, at, stem)
+    _close(lse.cpu().numpy(), g["lse"], lrt, lat, stem + " lse")
+
+
+@pytest.mark.parametrize("stem", [s for s in golden.stems("attention__")
+                                  if "_decode" in s or "nocausal" in s])
+def test_decode_matches_golden(pkg, dev, stem):
+    """The non-causal one-row cases are decode: every key visible."""
+    g = golden.load(stem)
+    q = torch.from_numpy(g["q"][0]).to(dev)
+    k, v = (torch.from_numpy(g[n]).to(dev) for n in ("k", "v"))
+    out = pkg.ops.attention_decode(q, k, v, _scale(q.shape[1]))
+    (rt, at), _ = _tol(k.shape[1])
+    _close(out.cpu().numpy().astype(np.float32), g["expected"][0], rt, at, stem)
+
+
+def _rand(rng, s_q, h, h_kv, s_kv, d, amp=1.0):
+    q = (rng.standard_normal((s_q, h, d)) * amp).astype(np.float16)
+    k = (rng.standard_normal((h_kv, s_kv, d)) * amp).astype(np.float16)
+    v = rng.standard_normal((h_kv, s_kv, d)).astype(np.float16)
+    return q, k, v
+
+
+@pytest.mark.parametrize("s_q,s_kv,off", [(256, 256, 0), (64, 320, 256)])
+def test_prefill_llama_shape_matches_oracle(pkg, dev, s_q, s_kv, off):
+    rng = np.random.default_rng(s_q + s_kv)
+    q, k, v = _rand(rng, s_q, 32, 8, s_kv, 128)
+    want, want_lse = oracle.attention(q, k, v, _scale(128), off, True)
+    out, lse = pkg.ops.attention(*(torch.from_numpy(a).to(dev) for a in (q, k, v)), _scale(128),
+                                 off, True, want_lse=True)
+    (rt, at), (lrt, lat) = _tol(s_kv)
+    _close(out.cpu().numpy().astype(np.float32), want.astype(np.float32), rt, at, "prefill")
+    _close(lse.cpu().numpy(), want_lse, lrt, lat, "prefill lse")
+
+
+@pytest.mark.parametrize("split_kv", [0, 1, 3, 7, 64])
+def test_decode_llama_shape_matches_oracle(pkg, dev, split_kv):
+    rng = np.random.default_rng(7)
+    kv_len = 4096
+    q, k, v = _rand(rng, 1, 32, 8, kv_len, 128)
+    want, _ = oracle.attention(q, k, v, _scale(128), 0, False)
+    qd, kd, vd = (torch.from_numpy(a).to(dev) for a in (q[0], k, v))
+    out = pkg.ops.attention_decode(qd, kd, vd, _scale(128), split_kv)
+    (rt, at), _ = _tol(kv_len)
+    _close(out.cpu().numpy().astype(np.float32), want[0].astype(np.float32), rt, at,
+           f"decode split_kv={split_kv}")
+    again = pkg.ops.attention_decode(qd, kd, vd, _scale(128), split_kv)
+    assert torch.equal(out, again)  # fixed-order merges: deterministic
+
+
+def test_empty_kv_and_unaligned_stride(pkg, dev):
+    c = pkg.cuda
+    q = torch.randn(3, 4, 64, device=dev).half()
+    out = torch.full_like(q, float("nan"))
+    lse = torch.zeros(3, 4, device=dev)
+    c.attention_prefill(q.data_ptr(), q.data_ptr(), q.data_ptr(), out.data_ptr(), 3, 0, 4, 2, 64,
+                        0, 0.125, 0, True, lse.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.zeros_like(out)) and bool(torch.isneginf(lse).all())
+    # KV heads 4 elements apart beyond s_kv * d: the stride is not a multiple of 8
+    rng = np.random.default_rng(3)
+    s_kv, d, h_kv = 40, 64, 2
+    stride = s_kv * d + 4
+    q, k, v = _rand(rng, 5, 4, h_kv, s_kv, d)
+    kp = np.zeros(h_kv * stride, np.float16)
+    vp = np.zeros(h_kv * stride, np.float16)
+    for hh in range(h_kv):
+        kp[hh * stride: hh * stride + s_kv * d] = k[hh].ravel()
+        vp[hh * stride: hh * stride + s_kv * d] = v[hh].ravel()
+    want, _ = oracle.attention(q, k, v, 0.125, 2, True)
+    qd, kd, vd = (torch.from_numpy(a).to(dev) for a in (q, kp, vp))
+    od = torch.empty_like(qd)
+    c.attention_prefill(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), 5, s_kv, 4,
+                        h_kv, d, stride, 0.125, 2, True, 0)
+    (rt, at), _ = _tol(s_kv)
+    _close(od.cpu().numpy().astype(np.float32), want.astype(np.float32), rt, at, "strided")
+
+
+def test_decode_throughput_llama8b(pkg, dev):
+    """Prints the decode kernel's HBM rate at Llama-3-8B, 4096 keys (not asserted)."""
+    H, H_kv, d, kv_len = 32, 8, 128, 4096
+    sets = [(torch.randn(H, d, device=dev).half(),
+             torch.randn(H_kv, kv_len, d, device=dev).half(),
+             torch.randn(H_kv, kv_len, d, device=dev).half()) for _ in range(8)]  # 134 MB
+    out = torch.empty(H, d, device=dev, dtype=torch.float16)
+    for s in sets[:3]:
+        pkg.ops.attention_decode(s[0], s[1], s[2])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 80
+    e0.record()
+    for it in range(n):
+        s = sets[it % len(sets)]
+        pkg.cuda.attention_decode(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), out.data_ptr(),
+                                  kv_len, H, H_kv, d, kv_len * d, d ** -0.5, 0,
+                                  torch.cuda.current_stream().cuda_stream)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / n * 1e3
+    byt = 2 * H_kv * kv_len * d * 2 + 2 * 2 * H * d
+    print(f"attention_decode Llama-3-8B kv_len=4096: {us:.1f} us, {byt / us / 1e3:.0f} GB/s")
