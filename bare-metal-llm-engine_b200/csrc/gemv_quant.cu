@@ -18,8 +18,10 @@
 //   blocks of a row: 1 KB of Q8_0 or 512 B of Q4_0 payload per warp step.
 // - Payload loads are 16-byte `ld.global.nc.L1::no_allocate`; scales (64 B per
 //   warp step) and x come through L1.
-// - The 32 products of a block are exact in FP32 (a 19-bit integer times a
-//   half); they are summed in FP32, multiplied by d and accumulated per lane.
+// - Weights are widened to exact FP16 values by bit arithmetic (no int->float
+//   conversion); the 32 products of a block are exact in FP32 (a half times a
+//   half) and are summed in FP32 by mixed-precision fma, multiplied by d and
+//   accumulated per lane.
 // - The warp shuffle and the cross-warp sum run in fixed order.
 // HBM bytes per weight: 1.0625 (Q8_0) or 0.5625 (Q4_0), against 2 for FP16.
 #include "common.cuh"
