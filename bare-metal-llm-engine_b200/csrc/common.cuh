@@ -1,9 +1,7 @@
 // common.cuh -- shared host and device machinery for the B200 hot-path library.
 //
-// Host side: the C-ABI error convention (status codes plus a thread-local
-// message, mirroring the reference's ENGINE_CHECK / CUDA_CHECK /
-// CUDA_CHECK_KERNEL in include/engine/check.hpp:36-107), device property
-// caches, and the driver entry point for TMA tensor-map encoding.
+// Host side: host.h (the C-ABI error convention, device property caches, the
+// TMA tensor-map encoder and the PDL launch helper), included here.
 //
 // Device side: thin inline-PTX wrappers for the sm_100a features the kernels
 // use -- mbarriers with BOUNDED waits, TMA tiled loads, tcgen05 (TMEM
