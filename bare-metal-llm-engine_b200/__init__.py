@@ -11,6 +11,10 @@ namespace engine::cuda) over the in-tree CUDA library ``libengine_b200.so``
   ENGINE_CHECK messages ("non-negative", "null", "eps").
 * ``ops`` -- the same calls on torch CUDA tensors (device memory and streams
   come from torch; the arithmetic is the library's).
+* ``tp`` -- the tensor-parallel layer set (one process per GPU) and the
+  library's NVLink communicator.
+* ``gguf`` -- the memory-mapped GGUF reader that places weights on the device
+  for these kernels.
 
 There is no CPU or library fallback: if the CUDA library is missing or fails
 to load, importing this package raises.
