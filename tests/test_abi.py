@@ -232,3 +232,38 @@ def test_quant_entries_reject_bad_arguments(pkg):
     _throws(pkg, c.gemv_q_nk, 4, P, 0, P, 0, P, 4, 32, substr="null")
     c.gemv_q_nk(8, P, P, P, 0, P, 0, 32)   # N == 0: no-op
     c.quant_repack(4, P, P, P, 0, 32)      # no rows: no-op
+
+
+def test_c_abi_links_and_runs_from_plain_c(pkg, tmp_path):
+    """include/engine_b200.h is C99 (pedantic, warnings as errors), and a plain C
+    program links libengine_b200.so and makes calls that need no GPU: the ABI
+    version, a rejected argument with its message, and a GGUF file that is not
+    one."""
+    pkg.lib()
+    src = tmp_path / "abi.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "engine_b200.h"
+int main(void) {
+  if (engine_abi_version() < 1) return 1;
+  engine_half_t* p = (engine_half_t*)16; /* never dereferenced: the call is rejected first */
+  if (engine_cuda_matmul_f16(p, p, p, -1, 4, 4, 0) != ENGINE_ERR_INVALID) return 2;
+  if (strstr(engine_last_error(), "non-negative") == NULL) return 3;
+  FILE* f = fopen("not.gguf", "wb");
+  fputs("this is not a gguf file, but it is long enough", f);
+  fclose(f);
+  engine_gguf_t* g = NULL;
+  if (engine_gguf_open("not.gguf", &g) != ENGINE_ERR_FORMAT || g != NULL) return 4;
+  puts("ok");
+  return 0;
+}
+''')
+    exe = tmp_path / "abi"
+    lib_dir = str(pkg.LIB_PATH.parent)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+                        f"-I{ROOT / 'include'}", str(src), "-o", str(exe), f"-L{lib_dir}",
+                        "-lengine_b200", f"-Wl,-rpath,{lib_dir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, cwd=tmp_path, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stdout, r.stderr)
