@@ -53,6 +53,7 @@ def _load_oracle():
         "orc_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f]),
         "orc_residual_rmsnorm": (None, [_p, _p, _p, _p, _p, _i64, _i64, _f]),
         "orc_attention": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i64, _i, _p]),
+        "orc_attention_online": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i64, _i, _p]),
         "orc_rmsnorm_linear": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f]),
         "orc_rmsnorm_linear_mt": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _i]),
         "orc_vector_add": (None, [_p, _p, _p, _i64]),
@@ -105,6 +106,7 @@ def ref_lib():
             "ref_rmsnorm": (None, [_p, _p, _p, _i64, _i64, _f]),
             "ref_residual_rmsnorm": (None, [_p, _p, _p, _p, _p, _i64, _i64, _f]),
             "ref_attention": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i64, _i, _p]),
+            "ref_attention_online": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _f, _i64, _i, _p]),
             "ref_rmsnorm_linear": (None, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _i]),
             "ref_swiglu_fp16": (None, [_p, _p, _p, _i64]),
             "ref_vector_add": (None, [_p, _p, _p, _i64]),
@@ -257,9 +259,10 @@ def rmsnorm_linear_f16(x, gamma, W, eps, residual=None, nthreads: int = 1, want_
     return (Y.view(np.float16), Y32) if want_f32 else Y.view(np.float16)
 
 
-def attention(q, k, v, scale, q_pos_offset=0, is_causal=True, ref=False):
-    """(out, lse) of src/cpu_ref/attention_cpu.cpp:87-155: q [s_q, n_heads, d],
-    k / v [n_kv_heads, s_kv, d] FP16 -> out FP16 [s_q, n_heads, d], lse FP32
+def attention(q, k, v, scale, q_pos_offset=0, is_causal=True, ref=False, online=False):
+    """(out, lse) of src/cpu_ref/attention_cpu.cpp:87-155 (online=True: the
+    tiled online-softmax form, :159-244): q [s_q, n_heads, d], k / v
+    [n_kv_heads, s_kv, d] FP16 -> out FP16 [s_q, n_heads, d], lse FP32
     [s_q, n_heads].  ref=True runs the reference's own compiled code instead."""
     q = _c(q, np.float16)
     k = _c(k, np.float16)
@@ -268,7 +271,10 @@ def attention(q, k, v, scale, q_pos_offset=0, is_causal=True, ref=False):
     n_kv, s_kv, _ = k.shape
     out = np.empty_like(q)
     lse = np.empty((s_q, n_heads), np.float32)
-    fn = ref_lib().ref_attention if ref else lib().orc_attention
+    if online:
+        fn = ref_lib().ref_attention_online if ref else lib().orc_attention_online
+    else:
+        fn = ref_lib().ref_attention if ref else lib().orc_attention
     rc = fn(_ptr(q), _ptr(k), _ptr(v), _ptr(out), s_q, s_kv, n_heads, n_kv, d, s_kv * d,
             float(scale), q_pos_offset, int(bool(is_causal)), _ptr(lse))
     if rc != 0:

@@ -414,6 +414,83 @@ int orc_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint1
   return 0;
 }
 
+/* The online-softmax form of the same attention, src/cpu_ref/attention_cpu.cpp:
+ * 159-244: keys in tiles of 16; per tile the FP64 scores and their max m_b,
+ * m' = max(m, m_b), alpha = exp(m - m') (0 while m = -inf), l and acc scaled by
+ * alpha, then p = exp(s - m') added to l and p * v to acc.  The recurrence a
+ * FlashAttention-2 kernel follows, in FP64.  Contract and empty handling as
+ * orc_attention. */
+int orc_attention_online(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                         int64_t s_q, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads,
+                         int64_t head_dim, int64_t kv_head_stride, float scale,
+                         int64_t q_pos_offset, int is_causal, float* out_lse) {
+  enum { kTile = 16 };
+  if (!q || !k || !v || !out) return 1;
+  if (s_q < 0 || s_kv < 0 || q_pos_offset < 0 || n_heads <= 0 || n_kv_heads <= 0) return 1;
+  if (n_heads % n_kv_heads != 0 || (head_dim != 64 && head_dim != 128) || !isfinite(scale))
+    return 1;
+  if (kv_head_stride < (s_kv > 0 ? s_kv * head_dim : 0)) return 1;
+  if (s_q == 0) return 0;
+  const uint16_t zero = orc_f32_to_f16(0.0f);
+  if (s_kv == 0) {
+    for (int64_t i = 0; i < s_q * n_heads * head_dim; ++i) out[i] = zero;
+    if (out_lse)
+      for (int64_t i = 0; i < s_q * n_heads; ++i) out_lse[i] = -INFINITY;
+    return 0;
+  }
+  const int64_t group = n_heads / n_kv_heads;
+  const double scale_d = (double)scale;
+  double tile[kTile];
+  double* acc = (double*)malloc((size_t)head_dim * sizeof(double));
+  if (!acc) return 1;
+  for (int64_t i = 0; i < s_q; ++i) {
+    int64_t max_j = s_kv - 1;
+    if (is_causal && q_pos_offset + i < max_j) max_j = q_pos_offset + i;
+    for (int64_t h = 0; h < n_heads; ++h) {
+      const int64_t row = i * n_heads + h;
+      const uint16_t* qr = q + row * head_dim;
+      uint16_t* orow = out + row * head_dim;
+      const uint16_t* kh = k + (h / group) * kv_head_stride;
+      const uint16_t* vh = v + (h / group) * kv_head_stride;
+      double m = -INFINITY, l = 0.0;
+      for (int64_t d = 0; d < head_dim; ++d) acc[d] = 0.0;
+      for (int64_t j0 = 0; j0 <= max_j; j0 += kTile) {
+        const int64_t j_end = (max_j + 1 < j0 + kTile) ? max_j + 1 : j0 + kTile;
+        double mb = -INFINITY;
+        for (int64_t j = j0; j < j_end; ++j) {
+          double dot = 0.0;
+          for (int64_t d = 0; d < head_dim; ++d)
+            dot += (double)orc_f16_to_f32(qr[d]) * (double)orc_f16_to_f32(kh[j * head_dim + d]);
+          tile[j - j0] = dot * scale_d;
+          if (tile[j - j0] > mb) mb = tile[j - j0];
+        }
+        if (isinf(mb) && mb < 0.0) continue;
+        const double mn = m > mb ? m : mb;
+        const double alpha = (isinf(m) && m < 0.0) ? 0.0 : exp(m - mn);
+        l *= alpha;
+        for (int64_t d = 0; d < head_dim; ++d) acc[d] *= alpha;
+        for (int64_t j = j0; j < j_end; ++j) {
+          const double p = exp(tile[j - j0] - mn);
+          l += p;
+          for (int64_t d = 0; d < head_dim; ++d)
+            acc[d] += p * (double)orc_f16_to_f32(vh[j * head_dim + d]);
+        }
+        m = mn;
+      }
+      if (l == 0.0) {
+        for (int64_t d = 0; d < head_dim; ++d) orow[d] = zero;
+        if (out_lse) out_lse[row] = -INFINITY;
+        continue;
+      }
+      const double inv = 1.0 / l;
+      for (int64_t d = 0; d < head_dim; ++d) orow[d] = orc_f32_to_f16((float)(acc[d] * inv));
+      if (out_lse) out_lse[row] = (float)(m + log(l));
+    }
+  }
+  free(acc);
+  return 0;
+}
+
 /* ------------------------------------------------- all-cores (row-split) forms */
 
 typedef struct {

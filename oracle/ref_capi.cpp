@@ -107,6 +107,21 @@ int ref_attention(const std::uint16_t* q, const std::uint16_t* k, const std::uin
   return 0;
 }
 
+int ref_attention_online(const std::uint16_t* q, const std::uint16_t* k, const std::uint16_t* v,
+                         std::uint16_t* out, std::int64_t s_q, std::int64_t s_kv,
+                         std::int64_t n_heads, std::int64_t n_kv_heads, std::int64_t head_dim,
+                         std::int64_t kv_head_stride, float scale, std::int64_t q_pos_offset,
+                         int is_causal, float* out_lse) {
+  try {
+    engine::cpu::attention_online(as_half(q), as_half(k), as_half(v), as_half(out), s_q, s_kv,
+                                  n_heads, n_kv_heads, head_dim, kv_head_stride, scale,
+                                  q_pos_offset, is_causal != 0, out_lse);
+  } catch (const std::exception&) {
+    return 1;
+  }
+  return 0;
+}
+
 void ref_vector_add(const float* a, const float* b, float* out, std::int64_t n) {
   engine::cpu::vector_add(a, b, out, n);
 }

@@ -78,11 +78,13 @@ def test_oracle_attention_matches_golden(stem):
     g = golden.load(stem)
     s_kv, d = g["k"].shape[1], g["q"].shape[2]
     p = next(c for c in golden._meta()["cases"] if c["stem"] == stem)["params"]
-    out, lse = oracle.attention(g["q"], g["k"], g["v"], 1.0 / np.float32(np.sqrt(np.float32(d))),
-                                p["q_pos_offset"], p["is_causal"])
     (rt, at), (lrt, lat) = _attention_tol(s_kv)
-    _close(out.astype(np.float32), g["expected"], rt, at)
-    _close(lse, g["lse"], lrt, lat)
+    for online in (False, True):
+        out, lse = oracle.attention(g["q"], g["k"], g["v"],
+                                    1.0 / np.float32(np.sqrt(np.float32(d))), p["q_pos_offset"],
+                                    p["is_causal"], online=online)
+        _close(out.astype(np.float32), g["expected"], rt, at)
+        _close(lse, g["lse"], lrt, lat)
 
 
 def test_golden_case_inventory():
@@ -169,10 +171,11 @@ def test_oracle_attention_bit_exact_vs_reference(s_q, s_kv, h, h_kv, d, off, cau
     k = (rng.standard_normal((h_kv, s_kv, d)) * amp).astype(np.float16)
     v = rng.standard_normal((h_kv, s_kv, d)).astype(np.float16)
     scale = 1.0 / np.sqrt(d)
-    a = oracle.attention(q, k, v, scale, off, causal)
-    b = oracle.attention(q, k, v, scale, off, causal, ref=True)
-    assert np.array_equal(a[0].view(np.uint16), b[0].view(np.uint16))
-    assert np.array_equal(a[1], b[1])
+    for online in (False, True):  # :87-155 and the tiled online form :159-244
+        a = oracle.attention(q, k, v, scale, off, causal, online=online)
+        b = oracle.attention(q, k, v, scale, off, causal, ref=True, online=online)
+        assert np.array_equal(a[0].view(np.uint16), b[0].view(np.uint16))
+        assert np.array_equal(a[1], b[1])
 
 
 @needs_ref
