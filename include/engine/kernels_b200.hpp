@@ -194,7 +194,10 @@ inline void gemv_q_nk(int qtype, const void* payload, const __half* scales, cons
                                            b200_detail::h(y), N, K, stream));
 }
 
-// kernels.hpp:153 / :191 -- attention
+// kernels.hpp:153 / :191 -- attention.  An engine build that keeps its own
+// kernels/attention_*.cu (for attention_naive and the *_with_mode variants,
+// which this library does not provide) defines ENGINE_B200_NO_ATTENTION.
+#ifndef ENGINE_B200_NO_ATTENTION
 inline void attention_prefill(const __half* q, const __half* k, const __half* v, __half* out,
                               std::int64_t s_q, std::int64_t s_kv, std::int64_t n_heads,
                               std::int64_t n_kv_heads, std::int64_t head_dim,
@@ -215,6 +218,7 @@ inline void attention_decode(const __half* q, const __half* k, const __half* v, 
       b200_detail::h(q), b200_detail::h(k), b200_detail::h(v), b200_detail::h(out), kv_len,
       n_heads, n_kv_heads, head_dim, kv_head_stride, scale, split_kv, stream));
 }
+#endif  // ENGINE_B200_NO_ATTENTION
 
 // -- tensor-parallel communicator (engine_tp_*) --------------------------------
 // One per rank, on the rank's current device.  The host exchanges handle()

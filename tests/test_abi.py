@@ -181,12 +181,25 @@ def test_last_error_is_per_thread(pkg):
 
 
 def test_cpp_adapter_header_compiles():
-    """include/engine/kernels_b200.hpp compiles as C++17 against the C ABI."""
-    src = '#include <engine/kernels_b200.hpp>\nint main(){return 0;}\n'
-    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", f"-I{ROOT / 'include'}",
-                        "-I/usr/local/cuda/include", "-x", "c++", "-"], input=src,
-                       capture_output=True, text=True)
-    assert r.returncode == 0, r.stderr
+    """include/engine/kernels_b200.hpp compiles as C++17 against the C ABI, with
+    and without its attention launchers (ENGINE_B200_NO_ATTENTION leaves them to
+    an engine that keeps its own attention sources)."""
+    for defs, uses_attention in (([], True), (["-DENGINE_B200_NO_ATTENTION"], False)):
+        body = ("engine::cuda::attention_decode(nullptr, nullptr, nullptr, nullptr, 0, 1, 1, "
+                "64, 0, 0.125f);" if uses_attention else "")
+        src = ('#include <engine/kernels_b200.hpp>\n'
+               f'int main(){{ {body} return 0; }}\n')
+        r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", *defs, f"-I{ROOT / 'include'}",
+                            "-I/usr/local/cuda/include", "-x", "c++", "-"], input=src,
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+    # with the macro the launchers are absent: a call no longer compiles
+    src = ('#include <engine/kernels_b200.hpp>\nint main(){ engine::cuda::attention_decode('
+           'nullptr, nullptr, nullptr, nullptr, 0, 1, 1, 64, 0, 0.125f); return 0; }\n')
+    r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-DENGINE_B200_NO_ATTENTION",
+                        f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", "-x", "c++", "-"],
+                       input=src, capture_output=True, text=True)
+    assert r.returncode != 0
 
 
 def test_tp_comm_rejects_bad_arguments(pkg):
