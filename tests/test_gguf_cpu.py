@@ -219,3 +219,91 @@ def test_lookups(pkg, tmp_path):
         d = ctypes.c_double()
         assert pkg.lib().engine_gguf_meta_float(h, b"llama.block_count", ctypes.byref(d)) == 1
         assert pkg.gguf.gemv_qtype(pkg.gguf.Q8_0) == 8 and pkg.gguf.gemv_qtype(pkg.gguf.Q4_0) == 4
+
+
+# ------------------------------------------------ property-based round trips
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+_INT_RANGES = {gw.UINT8: (0, 255), gw.INT8: (-128, 127), gw.UINT16: (0, 65535),
+               gw.INT16: (-32768, 32767), gw.UINT32: (0, 2 ** 32 - 1),
+               gw.INT32: (-2 ** 31, 2 ** 31 - 1), gw.UINT64: (0, 2 ** 63 - 1),
+               gw.INT64: (-2 ** 63, 2 ** 63 - 1)}
+
+
+def _scalar(vt):
+    if vt in _INT_RANGES:
+        lo, hi = _INT_RANGES[vt]
+        return st.integers(lo, hi)
+    if vt == gw.BOOL:
+        return st.booleans()
+    if vt == gw.FLOAT32:
+        return st.floats(width=32, allow_nan=False)
+    if vt == gw.FLOAT64:
+        return st.floats(allow_nan=False)
+    return st.text(max_size=12)  # STRING
+
+
+_SCALARS = sorted(_INT_RANGES) + [gw.BOOL, gw.FLOAT32, gw.FLOAT64, gw.STRING]
+
+
+@st.composite
+def _entry(draw, key):
+    if draw(st.integers(0, 3)) == 0:  # an array, sometimes of arrays
+        et = draw(st.sampled_from(_SCALARS + [gw.ARRAY]))
+        if et == gw.ARRAY:
+            inner = draw(st.sampled_from(_SCALARS))
+            items = draw(st.lists(st.lists(_scalar(inner), max_size=3).map(lambda x: (inner, x)),
+                                  max_size=3))
+        else:
+            items = draw(st.lists(_scalar(et), max_size=4))
+        return key, gw.ARRAY, (et, items)
+    vt = draw(st.sampled_from(_SCALARS))
+    return key, vt, draw(_scalar(vt))
+
+
+@st.composite
+def _model(draw):
+    keys = draw(st.lists(st.text("abcdefghij._", min_size=1, max_size=16), unique=True,
+                         max_size=8))
+    meta = [draw(_entry(k)) for k in keys]
+    names = draw(st.lists(st.text("abcdefghij.", min_size=1, max_size=12), unique=True,
+                          max_size=5))
+    tensors = []
+    for n in names:
+        ty = draw(st.sampled_from([gw.F32, gw.F16, gw.BF16, gw.Q8_0, gw.Q4_0]))
+        block, size = {gw.F32: (1, 4), gw.F16: (1, 2), gw.BF16: (1, 2), gw.Q8_0: (32, 34),
+                       gw.Q4_0: (32, 18)}[ty]
+        dims = tuple([block * draw(st.integers(1, 3))] +
+                     [draw(st.integers(1, 3)) for _ in range(draw(st.integers(0, 3)))])
+        nbytes = int(np.prod(dims)) // block * size
+        tensors.append((n, ty, dims, draw(st.binary(min_size=nbytes, max_size=nbytes))))
+    alignment = draw(st.sampled_from([8, 16, 32, 64, 256]))
+    version = draw(st.sampled_from([2, 3]))
+    return meta, tensors, alignment, version
+
+
+@settings(max_examples=150, deadline=None,
+          suppress_health_check=[HealthCheck.function_scoped_fixture, HealthCheck.too_slow])
+@given(m=_model())
+def test_round_trip_property(pkg, tmp_path, m):
+    meta, tensors, alignment, version = m
+    # (random keys use letters that cannot spell "general.alignment")
+    meta = list(meta) + ([("general.alignment", gw.UINT32, alignment)] if alignment != 32 else [])
+    blob, offsets = gw.build(meta, tensors, alignment=alignment, version=version)
+    path = _write(tmp_path, "p.gguf", blob)
+    with _open(pkg, path) as f:
+        assert f.version == version and f.alignment == alignment
+        md = f.metadata()
+        assert list(md) == [k for k, _, _ in meta]
+        for k, vt, v in meta:
+            if vt == gw.ARRAY:
+                assert md[k] == ("array", v[0], len(v[1]))
+            elif vt == gw.FLOAT32:
+                assert md[k] == float(np.float32(v))
+            else:
+                assert md[k] == (int(v) if vt == gw.BOOL else v)
+        assert [t.name for t in f.tensors] == [t[0] for t in tensors]
+        for (n, ty, dims, data), t in zip(tensors, f.tensors):
+            assert (t.type, t.dims, t.offset, t.nbytes) == (ty, dims, offsets[n], len(data))
+            assert bytes(f.data(n)) == data
