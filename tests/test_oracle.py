@@ -287,3 +287,66 @@ def test_multithreaded_oracle_is_bit_identical():
     X = rng.standard_normal((9, 64)).astype(np.float16)
     W = rng.standard_normal((31, 64)).astype(np.float16)
     assert np.array_equal(oracle.linear_f16(X, W, nthreads=1), oracle.linear_f16(X, W, nthreads=4))
+
+
+# ------------------------------------------- property-based pin, random shapes
+from hypothesis import given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+_dims = st.integers(1, 40)
+
+
+def _arr(seed, shape, dtype=np.float32, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(shape) * scale).astype(dtype)
+
+
+@needs_ref
+@settings(max_examples=60, deadline=None)
+@given(M=_dims, N=_dims, K=st.integers(0, 40), seed=st.integers(0, 2 ** 31))
+def test_property_matmul_and_gemv_fp16_bit_exact(M, N, K, seed):
+    A, B = _arr(seed, (M, K)), _arr(seed + 1, (K, N))
+    ref = np.empty((M, N), np.float32)
+    oracle.ref_lib().ref_matmul(_p(A), _p(B), _p(ref), M, N, K, 1)
+    assert np.array_equal(oracle.matmul(A, B), ref)
+    if K > 0:
+        Ah, xh = _arr(seed, (K, N), np.float16), _arr(seed + 2, K, np.float16)
+        refh = np.empty(N, np.float16)
+        oracle.ref_lib().ref_gemv_fp16(_p(Ah.view(np.uint16)), _p(xh.view(np.uint16)),
+                                       _p(refh.view(np.uint16)), N, K)
+        assert np.array_equal(oracle.gemv_fp16(Ah, xh).view(np.uint16), refh.view(np.uint16))
+
+
+@needs_ref
+@settings(max_examples=60, deadline=None)
+@given(M=_dims, N=_dims, K=_dims, with_w=st.booleans(), seed=st.integers(0, 2 ** 31))
+def test_property_rmsnorm_linear_and_residual_rmsnorm_bit_exact(M, N, K, with_w, seed):
+    import ctypes
+
+    x, W = _arr(seed, (M, K)), _arr(seed + 1, (K, N))
+    w = (_arr(seed + 2, K) * 0.1 + 1).astype(np.float32) if with_w else None
+    ref = np.empty((M, N), np.float32)
+    oracle.ref_lib().ref_rmsnorm_linear(_p(x), _p(w), _p(W), _p(ref), M, N, K, EPS, 1)
+    assert np.array_equal(oracle.rmsnorm_linear(x, w, W, EPS), ref)
+    r = _arr(seed + 3, (M, K))
+    norm, sm = oracle.residual_rmsnorm(x, r, w, EPS)
+    rn, rs = np.empty_like(x), np.empty_like(x)
+    oracle.ref_lib().ref_residual_rmsnorm(_p(x), _p(r), _p(w), _p(rn), _p(rs), ctypes.c_int64(M),
+                                          ctypes.c_int64(K), ctypes.c_float(EPS))
+    assert np.array_equal(norm, rn) and np.array_equal(sm, rs)
+
+
+@needs_ref
+@settings(max_examples=40, deadline=None)
+@given(s_q=st.integers(0, 9), s_kv=st.integers(0, 40), h_kv=st.sampled_from([1, 2]),
+       grp=st.sampled_from([1, 2, 4]), d=st.sampled_from([64, 128]), off=st.integers(0, 8),
+       causal=st.booleans(), amp=st.sampled_from([0.5, 1.0, 6.0]), online=st.booleans(),
+       seed=st.integers(0, 2 ** 31))
+def test_property_attention_bit_exact(s_q, s_kv, h_kv, grp, d, off, causal, amp, online, seed):
+    h = h_kv * grp
+    q = _arr(seed, (s_q, h, d), np.float16, amp)
+    k = _arr(seed + 1, (h_kv, s_kv, d), np.float16, amp)
+    v = _arr(seed + 2, (h_kv, s_kv, d), np.float16)
+    a = oracle.attention(q, k, v, d ** -0.5, off, causal, online=online)
+    b = oracle.attention(q, k, v, d ** -0.5, off, causal, ref=True, online=online)
+    assert np.array_equal(a[0].view(np.uint16), b[0].view(np.uint16))
+    assert np.array_equal(a[1], b[1])
