@@ -90,12 +90,12 @@ def shard_layer(full: dict, cfg: TPConfig, t: int, r: int) -> dict:
     """Slices one layer's full weights ({qkv, o, gate, up, down, attn_norm,
     ffn_norm}) into rank r's shard."""
     f = cfg.ffn // t
-    d = cfg.d_model // t
+    a = cfg.n_heads // t * cfg.head_dim  # O's input columns of this rank's query heads
     return {
         "attn_norm": full["attn_norm"],
         "ffn_norm": full["ffn_norm"],
         "qkv": full["qkv"][qkv_rows_for_rank(cfg, t, r)].contiguous(),
-        "o": full["o"][:, r * d:(r + 1) * d].contiguous(),
+        "o": full["o"][:, r * a:(r + 1) * a].contiguous(),
         "gate_up": torch.cat([full["gate"][r * f:(r + 1) * f], full["up"][r * f:(r + 1) * f]]).contiguous(),
         "down": full["down"][:, r * f:(r + 1) * f].contiguous(),
     }
@@ -287,7 +287,7 @@ def random_shards(cfg: TPConfig, rank: int, world: int, device, seed: int = 2026
     directly on the device; the same (seed, layer, rank) gives the same shard."""
     g = torch.Generator(device=device)
     f = cfg.ffn // world
-    d = cfg.d_model // world
+    a = cfg.n_heads // world * cfg.head_dim  # O's input columns: this rank's query heads
     qkv = cfg.qkv_rows // world
 
     def rn(shape, salt, scale=0.02, replicated=False):
@@ -303,7 +303,7 @@ def random_shards(cfg: TPConfig, rank: int, world: int, device, seed: int = 2026
             "attn_norm": gain(10 * l + 0),
             "ffn_norm": gain(10 * l + 1),
             "qkv": rn((qkv, cfg.d_model), 10 * l + 2),
-            "o": rn((cfg.d_model, d), 10 * l + 3),
+            "o": rn((cfg.d_model, a), 10 * l + 3),
             "gate_up": rn((2 * f, cfg.d_model), 10 * l + 4),
             "down": rn((cfg.d_model, f), 10 * l + 5),
         })
@@ -315,15 +315,20 @@ def random_shards(cfg: TPConfig, rank: int, world: int, device, seed: int = 2026
     return layers, lm, embed, final_norm
 
 
+def _layer_weights(cfg: TPConfig) -> int:
+    """Elements of one layer's projections: QKV, O (d_model x the query heads'
+    width), gate and up, down."""
+    return (cfg.qkv_rows * cfg.d_model + cfg.d_model * cfg.n_heads * cfg.head_dim +
+            2 * cfg.ffn * cfg.d_model + cfg.d_model * cfg.ffn)
+
+
 def weight_bytes_per_rank(cfg: TPConfig, world: int) -> float:
-    per_layer = (cfg.qkv_rows * cfg.d_model + cfg.d_model * cfg.d_model +
-                 2 * cfg.ffn * cfg.d_model + cfg.d_model * cfg.ffn) / world
+    per_layer = _layer_weights(cfg) / world
     return 2.0 * (cfg.n_layers * per_layer + cfg.vocab * cfg.d_model / world)
 
 
 def flops_per_token(cfg: TPConfig) -> float:
-    per_layer = (cfg.qkv_rows * cfg.d_model + cfg.d_model * cfg.d_model +
-                 2 * cfg.ffn * cfg.d_model + cfg.d_model * cfg.ffn)
+    per_layer = _layer_weights(cfg)
     return 2.0 * (cfg.n_layers * per_layer + cfg.vocab * cfg.d_model)
 
 

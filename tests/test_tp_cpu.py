@@ -51,7 +51,7 @@ def run_model(tp, cfg, world, rank, ops, group=None):
     return x, nxt, m.allreduce_count
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, cfg_kw=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -62,7 +62,7 @@ def _worker(rank, world, port, q):
         from tests.tp_cpu_ops import CpuOps
 
         tp = pkg.tp
-        cfg = tp.TPConfig(**CFG_KW)
+        cfg = tp.TPConfig(**(cfg_kw or CFG_KW))
         x, nxt, n_ar = run_model(tp, cfg, world, rank, CpuOps())
         q.put((rank, x.numpy(), nxt.numpy(), n_ar))
     except Exception as e:  # report instead of hanging the parent
@@ -79,19 +79,23 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_tp_layer_set_matches_unsharded_on_gloo(world):
+# d_model need not equal n_heads * head_dim: O's input is the query heads
+GEMMA_LIKE_KW = dict(CFG_KW, d_model=48)
+
+
+@pytest.mark.parametrize("world,cfg_kw", [(2, CFG_KW), (4, CFG_KW), (2, GEMMA_LIKE_KW)])
+def test_tp_layer_set_matches_unsharded_on_gloo(world, cfg_kw):
     pkg = load_package()
     from tests.tp_cpu_ops import CpuOps
 
     tp = pkg.tp
-    cfg = tp.TPConfig(**CFG_KW)
+    cfg = tp.TPConfig(**cfg_kw)
     x1, n1, ar1 = run_model(tp, cfg, 1, 0, CpuOps())
     assert ar1 == 0
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, cfg_kw)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in range(world)]
@@ -203,3 +207,54 @@ def test_tp_peer_failure_is_an_error_not_a_hang(mode):
     assert t0 < PG_TIMEOUT_S + 60, f"rank 0 took {t0:.0f} s to notice"
     assert res[1][0] in ({"never_joins": "absent", "exits_early": "exited"}.get(mode) or
                          "error: RuntimeError('failure injected on rank 1')",)
+
+
+# ------------------------------------------------ sharding properties
+from hypothesis import given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+
+@st.composite
+def _cfg_and_degree(draw):
+    t = draw(st.sampled_from([1, 2, 4, 8]))
+    kv = t * draw(st.integers(1, 2))
+    h = kv * draw(st.integers(1, 3))
+    hd = draw(st.sampled_from([2, 4, 6]))
+    # d_model need not equal n_heads * head_dim (Gemma-style shapes)
+    d = t * draw(st.integers(1, 4))
+    return dict(d_model=d, n_heads=h, n_kv_heads=kv, head_dim=hd, ffn=t * draw(st.integers(1, 4)),
+                n_layers=1, vocab=t * draw(st.integers(1, 5)), eps=1e-5), t
+
+
+@settings(max_examples=80, deadline=None)
+@given(ct=_cfg_and_degree())
+def test_shards_partition_every_weight(ct):
+    """Over the ranks, the shards of every weight reassemble it exactly: QKV rows
+    (head-aligned), O columns (the rank's query heads), gate and up rows, down
+    columns and the vocab rows of the LM head."""
+    kw, t = ct
+    tp = load_package().tp
+    cfg = tp.TPConfig(**kw)
+    cfg.check(t)
+    hd_all = cfg.n_heads * cfg.head_dim
+    g = torch.Generator().manual_seed(1)
+    full = {"attn_norm": torch.randn(cfg.d_model, generator=g),
+            "ffn_norm": torch.randn(cfg.d_model, generator=g),
+            "qkv": torch.randn(cfg.qkv_rows, cfg.d_model, generator=g),
+            "o": torch.randn(cfg.d_model, hd_all, generator=g),
+            "gate": torch.randn(cfg.ffn, cfg.d_model, generator=g),
+            "up": torch.randn(cfg.ffn, cfg.d_model, generator=g),
+            "down": torch.randn(cfg.d_model, cfg.ffn, generator=g)}
+    lm = torch.randn(cfg.vocab, cfg.d_model, generator=g)
+    shards = [tp.shard_layer(full, cfg, t, r) for r in range(t)]
+    rows = torch.cat([tp.qkv_rows_for_rank(cfg, t, r) for r in range(t)])
+    assert torch.equal(rows.sort().values, torch.arange(cfg.qkv_rows))
+    assert torch.equal(torch.cat([s["qkv"] for s in shards]), full["qkv"][rows])
+    assert torch.equal(torch.cat([s["o"] for s in shards], dim=1), full["o"])
+    f = cfg.ffn // t
+    assert torch.equal(torch.cat([s["gate_up"][:f] for s in shards]), full["gate"])
+    assert torch.equal(torch.cat([s["gate_up"][f:] for s in shards]), full["up"])
+    assert torch.equal(torch.cat([s["down"] for s in shards], dim=1), full["down"])
+    assert torch.equal(torch.cat([tp.shard_head(lm, cfg, t, r) for r in range(t)]), lm)
+    for s in shards:  # each rank's q rows are whole heads, and its O input matches them
+        assert s["o"].shape[1] == cfg.n_heads // t * cfg.head_dim
