@@ -280,3 +280,37 @@ int main(void) {
     assert r.returncode == 0, r.stderr
     r = subprocess.run([str(exe)], capture_output=True, text=True, cwd=tmp_path, timeout=60)
     assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stdout, r.stderr)
+
+
+# ------------------------------------------------ property: validation first
+from hypothesis import given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+# entry point -> (pointer argument required?, number of dims); optional pointers
+# (residual, gamma, weight, lse) may be null.  Every call below is invalid by
+# construction (a negative dimension or a null required pointer), so none can
+# reach a kernel launch, on any machine.
+_CALLS = {
+    "matmul_f16": ([True, True, True], 3),
+    "linear_f16": ([True, True, False, True], 3),
+    "gemv_f16_nk": ([True, True, False, True], 2),
+    "rmsnorm_linear_f16": ([True, False, True, False, True], 3),
+    "matmul_register_tiled": ([True, True, True], 3),
+    "gemv": ([True, True, True], 2),
+    "gemv_fp16": ([True, True, True], 2),
+}
+
+
+@settings(max_examples=150, deadline=None)
+@given(name=st.sampled_from(sorted(_CALLS)), data=st.data())
+def test_property_invalid_arguments_are_rejected_before_any_device_work(pkg, name, data):
+    req, ndims = _CALLS[name]
+    ptrs = [data.draw(st.sampled_from([0, P])) for _ in req]
+    dims = [data.draw(st.integers(-3, 6)) for _ in range(ndims)]
+    if all(p for p, r in zip(ptrs, req) if r) and min(dims) >= 0:
+        dims[data.draw(st.integers(0, ndims - 1))] = -1  # make it invalid
+    fn = getattr(pkg.cuda, name)
+    args = ptrs + dims + ([1e-5] if name == "rmsnorm_linear_f16" else [])
+    with pytest.raises(pkg.EngineError) as ei:
+        fn(*args)
+    assert ei.value.code == 1 and str(ei.value)
