@@ -397,7 +397,9 @@ ENGINE_B200_API int engine_gguf_meta_string(const engine_gguf_t* g, const char* 
  *    engine_cuda_gemv_q_nk, with K = dims[0] and N = the product of the others.
  * The host copy goes through pinned double buffers owned by the handle; the
  * call returns once the copy and the repack are enqueued on `stream`, and the
- * mapping must stay open until they finish.  Other types: ENGINE_ERR_UNSUPPORTED. */
+ * mapping must stay open until they finish.  Other types: ENGINE_ERR_UNSUPPORTED.
+ * One handle's pinned buffers serve one load at a time: calls on the same
+ * handle from several host threads must be serialised by the caller. */
 ENGINE_B200_API int engine_gguf_load_tensor(engine_gguf_t* g, int64_t index, void* payload,
                                             engine_half_t* scales, void* staging,
                                             engine_stream_t stream);
