@@ -396,8 +396,9 @@ ENGINE_B200_API int engine_gguf_meta_string(const engine_gguf_t* g, const char* 
  *    and engine_cuda_quant_repack writes `payload` and `scales` for
  *    engine_cuda_gemv_q_nk, with K = dims[0] and N = the product of the others.
  * The host copy goes through pinned double buffers owned by the handle; the
- * call returns once the copy and the repack are enqueued on `stream`, and the
- * mapping must stay open until they finish.  Other types: ENGINE_ERR_UNSUPPORTED.
+ * call returns once the copy and the repack are enqueued on `stream`
+ * (engine_gguf_close waits for this handle's copies before freeing the
+ * buffers).  Other types: ENGINE_ERR_UNSUPPORTED.
  * One handle's pinned buffers serve one load at a time: calls on the same
  * handle from several host threads must be serialised by the caller. */
 ENGINE_B200_API int engine_gguf_load_tensor(engine_gguf_t* g, int64_t index, void* payload,
