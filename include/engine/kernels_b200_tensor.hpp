@@ -5,8 +5,9 @@
 // The engine keeps raw pointers at the kernel boundary and plans Tensor-aware
 // overloads "as thin wrappers that unpack .data() and .shape() and forward"
 // (include/engine/kernels.hpp:16-17, ADR 0003).  These are those wrappers for
-// every launcher of this library: same names, the engine's Tensor
-// (include/engine/tensor.hpp) in place of pointer + dims, stream last.
+// the GEMM, GEMV, norm, norm->projection, SwiGLU and vector-add launchers of
+// this library: same names, the engine's Tensor (include/engine/tensor.hpp) in
+// place of pointer + dims, stream last.
 //
 // Each wrapper checks its tensors before forwarding: for every argument in
 // turn, defined (an undefined Tensor is allowed only where the pointer API
