@@ -157,9 +157,24 @@ __device__ __forceinline__ void store16(void* p, int64_t i, float v) {
   }
 }
 
+// Tile-order group: tiles are walked G row-tiles at a time so B tiles are reused
+// from L2.  A compile-time tunable (the default is the measured best).
+#ifndef ENGINE_TC_GROUP
+#define ENGINE_TC_GROUP 8
+#endif
+// 2-SM kernel: shared-memory stages (0 = the default for the tile width) and the
+// distance, in k-blocks, of its L2 prefetch of operand tiles ahead of the TMA
+// loads (0 = off).
+#ifndef ENGINE_TC2_STAGES
+#define ENGINE_TC2_STAGES 0
+#endif
+#ifndef ENGINE_TC2_L2PF
+#define ENGINE_TC2_L2PF 0
+#endif
+
 __device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm,
                                             int& tn) {
-  constexpr int G = 8;  // walk G row-tiles at a time so B tiles are reused from L2
+  constexpr int G = ENGINE_TC_GROUP;
   const int64_t per_group = static_cast<int64_t>(G) * tiles_n;
   const int64_t group = t / per_group;
   const int first_m = static_cast<int>(group * G);
@@ -736,7 +751,7 @@ struct Tc2Cfg {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 rows of A
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's BN/2 rows / columns of B
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN >= 256) ? 6 : 8;
+  static constexpr int kStages = ENGINE_TC2_STAGES > 0 ? ENGINE_TC2_STAGES : ((BN >= 256) ? 6 : 8);
   static constexpr int kTmemCols = pow2_at_least(2 * BN);
   static constexpr int kEpiBytes = 2 * kEpiStageBytes;  // TMA-store staging
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 256 + 1024;
@@ -818,6 +833,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + s * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kABytes;
+          if constexpr (ENGINE_TC2_L2PF > 0) {
+            // Warm L2 with this CTA's operand tiles ENGINE_TC2_L2PF k-blocks ahead,
+            // so that the first reader of a panel slice waits on L2, not DRAM.
+            const int64_t kp = kb + ENGINE_TC2_L2PF;
+            if (kp < w.kb1) {
+              tma_prefetch_2d(&tmA, static_cast<int32_t>(kp * kBK),
+                              tm * 256 + static_cast<int>(rank) * 128);
+              if constexpr (B_MN) {
+#pragma unroll
+                for (int j = 0; j < BN / 128; ++j)
+                  tma_prefetch_2d(&tmB, tn * BN + static_cast<int>(rank) * (BN / 2) + j * 64,
+                                  static_cast<int32_t>(kp * kBK));
+              } else {
+                tma_prefetch_2d(&tmB, static_cast<int32_t>(kp * kBK),
+                                tn * BN + static_cast<int>(rank) * (BN / 2));
+              }
+            }
+          }
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
           const uint32_t fbar = full_leader0 + s * 8;
           tma_load_2d_2sm(sa, &tmA, fbar, static_cast<int32_t>(kb * kBK),
@@ -1293,8 +1326,9 @@ int gemm_tc_dispatch(const void* A, const void* B, const void* residual, void* C
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
   p.tma_epi = 0;
+  static const int tma_epi_env = env_int("ENGINE_TC_TMA_EPI", 1);
   auto enable_tma_out = [&]() {
-    if (!resid && (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
+    if (tma_epi_env != 0 && !resid && (N % 8 == 0) && (reinterpret_cast<uintptr_t>(C) % 16 == 0) &&
         make_tmap_2d(&tc, C, dt, 2, static_cast<uint64_t>(M), static_cast<uint64_t>(N),
                      static_cast<uint64_t>(N), 128, 64)) {
       p.tma_epi = 1;

@@ -423,6 +423,244 @@ def bench_main(args, metric: str) -> int:
     return 0
 
 
+def full_random_weights(cfg: TPConfig, device, seed: int = 11, dtype=torch.float16):
+    """Unsharded random weights drawn on `device` from a seeded device generator:
+    every GPU draws the same values for the same seed, so each rank can shard
+    them itself (the parity check of the sharded layer set against t = 1)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def rn(*shape, scale=0.02):
+        return (torch.randn(*shape, device=device, generator=g) * scale).to(dtype)
+
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "attn_norm": (1 + rn(cfg.d_model, scale=0.1).float()).to(dtype),
+            "ffn_norm": (1 + rn(cfg.d_model, scale=0.1).float()).to(dtype),
+            "qkv": rn(cfg.qkv_rows, cfg.d_model),
+            "o": rn(cfg.d_model, cfg.n_heads * cfg.head_dim),
+            "gate": rn(cfg.ffn, cfg.d_model),
+            "up": rn(cfg.ffn, cfg.d_model),
+            "down": rn(cfg.d_model, cfg.ffn),
+        })
+    lm = rn(cfg.vocab, cfg.d_model)
+    embed = rn(cfg.vocab, cfg.d_model, scale=1.0)
+    fnorm = (1 + rn(cfg.d_model, scale=0.1).float()).to(dtype)
+    return layers, lm, embed, fnorm
+
+
+# Parity headroom of the t = N layer set against t = 1: each op is pinned to the
+# oracle by its own test; the chains differ only in rounding (every rank rounds
+# its partial projection to FP16 before the sum at t > 1, t = 1 rounds once).
+# One FP16 ulp at the hidden state's magnitude (|x| < 8) is <= 2^-8; a few ulps
+# per op over a two-layer chain stay inside 2e-2 absolute + 2e-2 relative, the
+# same kind of documented headroom the reference uses for stacked layers
+# (tests/test_kernels.cu:3387-3390).
+TP_PARITY_ATOL = 2e-2
+TP_PARITY_RTOL = 2e-2
+TP_PARITY_TOKENS = (0, 5, 128255, 4242)
+
+
+def _max_over_ranks(x: float, world: int, dev) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def tp_parity(cfg: TPConfig, world: int, rank: int, dev, comm=None) -> dict:
+    """The t = N layer set (two layers, the product's own sharding) against t = 1
+    on the same weights: every rank's hidden state and logits shard, once with
+    NCCL all-reduces and once with the NVLink communicator when given.  Rank 0
+    computes t = 1 and broadcasts it.  Returns {"ok", "max_abs_err", ...}, the
+    same on every rank."""
+    import dataclasses
+
+    pcfg = dataclasses.replace(cfg, n_layers=2)
+    layers, lm, embed, fnorm = full_random_weights(pcfg, dev)
+    ids = torch.tensor(TP_PARITY_TOKENS, dtype=torch.int32, device=dev)
+    shards = [shard_layer(L, pcfg, world, rank) for L in layers]
+    m = TPLayerSet(pcfg, rank, world, shards, shard_head(lm, pcfg, world, rank), embed, fnorm)
+    ops = m.ops
+    B = len(TP_PARITY_TOKENS)
+    ref_x = torch.empty(B, pcfg.d_model, device=dev, dtype=torch.float16)
+    ref_l = torch.empty(B, pcfg.vocab, device=dev, dtype=torch.float16)
+    if rank == 0:
+        m1 = TPLayerSet(pcfg, 0, 1, [shard_layer(L, pcfg, 1, 0) for L in layers], lm, embed, fnorm)
+        x1 = m1.hidden(ops.embedding(embed, ids))
+        ref_x.copy_(x1)
+        ref_l.copy_(m1.logits_shard(x1))
+        del m1
+    if world > 1:
+        dist.broadcast(ref_x, 0)
+        dist.broadcast(ref_l, 0)
+    v = pcfg.vocab // world
+    want_l = ref_l[:, rank * v:(rank + 1) * v].float()
+    res = {"ok": True, "max_abs_err": 0.0, "layers": pcfg.n_layers, "tokens": B,
+           "atol": TP_PARITY_ATOL, "rtol": TP_PARITY_RTOL, "collectives": []}
+    for name, c in (("nccl", None), ("nvlink", comm)):
+        if name == "nvlink" and (c is None or world == 1):
+            continue
+        m.comm = c
+        m.allreduce_count = 0
+        x = m.hidden(ops.embedding(embed, ids))
+        lg = m.logits_shard(x)
+        err_x = (x.float() - ref_x.float()).abs()
+        err_l = (lg.float() - want_l).abs()
+        ok = bool((err_x <= TP_PARITY_ATOL + TP_PARITY_RTOL * ref_x.float().abs()).all() and
+                  (err_l <= TP_PARITY_ATOL + TP_PARITY_RTOL * want_l.abs()).all() and
+                  m.allreduce_count == (2 * pcfg.n_layers if world > 1 else 0))
+        bad = _max_over_ranks(0.0 if ok else 1.0, world, dev)
+        err = _max_over_ranks(max(err_x.max().item(), err_l.max().item()), world, dev)
+        res["ok"] = res["ok"] and bad == 0.0
+        res["max_abs_err"] = max(res["max_abs_err"], err)
+        res["collectives"].append(name)
+    m.comm = None
+    return res
+
+
+def _time_tp_step(model, ids, steps: int, warmup: int, graph: bool, world: int, dev) -> float:
+    """ms per step of model.step(ids), max over ranks; the whole step in one CUDA
+    graph when `graph` (released before returning)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        model.step(ids)
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            model.step(ids)
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            model.step(ids)
+        torch.cuda.synchronize()
+        for _ in range(2):
+            g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        if g is not None:
+            g.replay()
+        else:
+            model.step(ids)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+
+
+def _time_calls(fn, calls: int, world: int, dev, graph: bool = True) -> float:
+    """us per call of fn() (CUDA graph of `calls` calls when `graph`), max over ranks."""
+    stream = torch.cuda.current_stream()
+    s = torch.cuda.Stream()
+    s.wait_stream(stream)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    if g is not None:
+        g.replay()
+    else:
+        for _ in range(calls):
+            fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return _max_over_ranks(e0.elapsed_time(e1) * 1e3 / calls, world, dev)
+
+
+def bench_tp_block(steps: int, warmup: int, hbm_peak: float, tensor_peak: float,
+                   peak_kind: str) -> dict:
+    """The Llama-3-8B-shaped tensor-parallel layer set at t = the process group's
+    size (1 without one), for bench.py's JSON line: decode B = 1 and B = 32 (one
+    CUDA graph per step; the library's NVLink communicator fused into O / down
+    at t > 1), prefill S = 2048 (NCCL all-reduces), the all-reduces alone, and
+    the t = N vs t = 1 parity check.  Every rank takes the same steps; the
+    figures are max over ranks."""
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = LLAMA3_8B
+    comm = NvlinkComm(rank, world, 32 * cfg.d_model) if world > 1 else None
+    out = {"t": world, "model": "llama3-8b-shaped", "layers": cfg.n_layers,
+           "attention": "stand-in (out of scope)",
+           "nccl_ranks": dist.get_world_size() if dist.is_initialized() else 0,
+           "collective_decode": ("nvlink one-shot all-reduce fused into the O / down projection"
+                                 if comm is not None else "none (t = 1)"),
+           "collective_prefill": "nccl all_reduce" if world > 1 else "none (t = 1)",
+           "peak_kind": peak_kind}
+    if world > 1:
+        out["parity"] = tp_parity(cfg, world, rank, dev, comm)
+        out["parity_ok"] = out["parity"]["ok"]
+    else:
+        out["parity_ok"] = None
+        out["parity"] = "t = 1 is the reference of the t = N check"
+    torch.cuda.empty_cache()
+    layers, lm, embed, fnorm = random_shards(cfg, rank, world, dev)
+    wbytes = weight_bytes_per_rank(cfg, world)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    for B in (1, 32):
+        model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=comm)
+        ids = torch.randint(0, cfg.vocab, (B,), device=dev, generator=gen, dtype=torch.int32)
+        if world > 1:
+            dist.broadcast(ids, 0)
+        ms = _time_tp_step(model, ids, max(steps, 10), warmup, True, world, dev)
+        gbs = wbytes / (ms * 1e-3) / 1e9
+        out[f"decode_b{B}"] = {"ms_per_step": ms, "tokens_s": B / (ms * 1e-3),
+                               "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / hbm_peak}
+    # prefill S = 2048, eager (16 MiB all-reduces over NCCL)
+    S = 2048
+    model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=None)
+    ids = torch.randint(0, cfg.vocab, (S,), device=dev, generator=gen, dtype=torch.int32)
+    if world > 1:
+        dist.broadcast(ids, 0)
+    ms = _time_tp_step(model, ids, max(3, min(steps, 8)), min(warmup, 3), False, world, dev)
+    tf = flops_per_token(cfg) * S / world / (ms * 1e-3) / 1e12
+    out["prefill_s2048"] = {"ms_per_step": ms, "tokens_s": S / (ms * 1e-3),
+                            "tflops_per_gpu": tf, "tensor_frac_per_gpu": tf / tensor_peak}
+    # The all-reduces alone at the step's message sizes (64 per step), for the share.
+    if world > 1:
+        calls = 2 * cfg.n_layers
+        for B in (1, 32):
+            P = torch.randn(B * cfg.d_model, device=dev, generator=gen).half()
+            Y = torch.empty_like(P)
+            us = _time_calls(lambda: comm.allreduce(P, out=Y), calls, world, dev)
+            out[f"decode_b{B}"]["allreduce_us"] = us
+            out[f"decode_b{B}"]["allreduce_share_est"] = calls * us * 1e-3 / out[f"decode_b{B}"]["ms_per_step"]
+        P = torch.randn(S * cfg.d_model, device=dev, generator=gen).half()
+        us = _time_calls(lambda: dist.all_reduce(P), 8, world, dev, graph=False)
+        out["prefill_s2048"]["allreduce_us"] = us
+        out["prefill_s2048"]["allreduce_share_est"] = calls * us * 1e-3 / out["prefill_s2048"]["ms_per_step"]
+        del P, Y
+    del model, layers, lm, embed, fnorm
+    if comm is not None:
+        comm.close()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
 def bench_collectives(args) -> int:
     """bench.py --workload tp-comm (one process per GPU, world >= 2): device time
     per call of the row-split projection + all-reduce at the decode shapes,

@@ -143,6 +143,10 @@ class ClockSampler:
             except Exception:
                 pass
 
+    def median(self):
+        """Median SM MHz of the samples (None without NVML or samples)."""
+        return statistics.median(self.samples) if (self._h is not None and self.samples) else None
+
     def summary(self):
         if self._h is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
@@ -226,10 +230,13 @@ def environment(with_gpu: bool) -> dict:
 
 
 def headline_config(world: int) -> dict:
-    """The workload both arms quote (the reference arm adds how it ran it)."""
+    """The workload both arms quote, identical on both (how the reference arm ran
+    it is a separate top-level key of its line)."""
     return {"workload": "FP16 GEMM C[4096,4096] = A[4096,4096] B[4096,4096] (FP32 accumulate) "
                         "+ decode GEMV W[4096,14336] x",
-            "M": 4096, "N": 4096, "K": 4096, "parallelism": f"replicas x{world}"}
+            "M": 4096, "N": 4096, "K": 4096, "parallelism": f"replicas x{world}",
+            "l2": "rotating operand pools larger than the 126 MB L2 "
+                  "(4 x 96 MiB GEMM sets, 4 x 112 MiB GEMV weights)"}
 
 
 def cpu_single_thread(cpu_seconds: float) -> dict:
@@ -302,8 +309,9 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (fp64 accumulate)", "data": "synthetic",
-        "config": dict(headline_config(world), implementation="the reference's CPU code, "
-                       "a row sample of the GEMM per step"),
+        "config": headline_config(world),
+        "implementation": "the reference's CPU code (engine::cpu::matmul), a row sample of the "
+                          "GEMM per step",
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nthreads, "kind": kind,
                          "sample": sample, "single_thread": cpu_single_thread(4.0)},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -336,12 +344,13 @@ def time_launches(torch, fn, sets, steps, warmup, stream):
     return per, t0.elapsed_time(t1)
 
 
-def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False):
+def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False, min_ms=0.0):
     """Captures `steps` launches (rotating operand sets) in one CUDA graph and
-    times `reps` replays with CUDA events on the replay stream; returns the
-    median ms per launch, or with stats=True {"median", "q1", "q3"} over the
-    replays.  Launch-bound kernels (~5-25 us) are timed without host enqueue
-    gaps."""
+    times at least `reps` replays -- more, until `min_ms` of device time has
+    passed, so a clock sampler sees the kernel under load -- with CUDA events on
+    the replay stream; returns the median ms per launch, or with stats=True
+    {"median", "q1", "q3"} over the replays.  Launch-bound kernels (~5-25 us)
+    are timed without host enqueue gaps."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
@@ -356,7 +365,7 @@ def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False):
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     per = []
-    for _ in range(max(reps, 1)):
+    while len(per) < max(reps, 1) or sum(per) * steps < min_ms:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(s)
@@ -364,6 +373,8 @@ def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False):
         e1.record(s)
         torch.cuda.synchronize()
         per.append(e0.elapsed_time(e1) / steps)
+        if len(per) >= 400:
+            break
     del g
     med = statistics.median(per)
     if not stats:
@@ -372,10 +383,38 @@ def time_graph(torch, fn, sets, steps, warmup, reps=5, stats=False):
     return {"median": med, "q1": q[0], "q3": q[2]}
 
 
-def secondary_configs(torch, pkg, dev, g, world, args):
-    """The other BASELINE configurations, one line each (CUDA-graph timing,
-    operand pools larger than L2)."""
+def secondary_configs(torch, pkg, dev, g, world, args, local=0):
+    """The other BASELINE configurations, one entry each: CUDA-graph timing over
+    operand pools larger than L2, the median SM clock sampled while each one
+    runs ("mhz") and, for the HBM-bound lines, the time in clock cycles
+    ("kcyc" = us x MHz / 1000), which separates a slower clock from a slower
+    kernel."""
     out = {}
+
+    def timed(name, fn, sets, steps, warmup, byt=None, flops=None, extra=None):
+        with ClockSampler(local, period_s=0.001) as clk:
+            ms = time_graph(torch, fn, sets, steps, warmup, min_ms=30.0)
+        d = {"us": ms * 1e3, "mhz": clk.median()}
+        if byt is not None:
+            d["gbs"] = byt / (ms * 1e-3) / 1e9
+            if d["mhz"]:
+                d["kcyc"] = ms * 1e3 * d["mhz"] / 1e3
+        if flops is not None:
+            d["tflops"] = flops / (ms * 1e-3) / 1e12
+        if extra:
+            d.update(extra)
+        out[name] = d
+
+    # Config 2: the other two decode GEMV shapes (rotating pools > L2), first in
+    # the sequence, beside the headline shape measured just before
+    for (N, K, nsets) in ((4096, 4096, 6), (14336, 4096, 4)):
+        sets = [((torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        fn = lambda s, st, N=N, K=K: pkg.cuda.gemv_f16_nk(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), N, K, st)
+        timed(f"gemv_{N}x{K}", fn, sets, 60, 5, byt=2.0 * (N * K + K + N))
+        del sets
     # Config 3: fused RMSNorm -> QKV, W[6144,4096], B in {1, 16}
     N, K = 6144, 4096
     pool = [(torch.randn(16, K, device=dev, generator=g).half(),
@@ -385,35 +424,8 @@ def secondary_configs(torch, pkg, dev, g, world, args):
     for B in (1, 16):
         fn = lambda s, st, B=B: pkg.cuda.rmsnorm_linear_f16(  # noqa: E731
             s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0, s[3].data_ptr(), B, N, K, 1e-5, st)
-        ms = time_graph(torch, fn, pool, 100, 5)
-        byt = 2.0 * (N * K + B * K + K + B * N)
-        out[f"rmsnorm_qkv_b{B}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9}
+        timed(f"rmsnorm_qkv_b{B}", fn, pool, 100, 5, byt=2.0 * (N * K + B * K + K + B * N))
     del pool
-    # Config 4b: X[S,4096] W[14336,4096]^T
-    N, K = 14336, 4096
-    Ws = [(torch.randn(N, K, device=dev, generator=g) * 0.02).half() for _ in range(2)]
-    for S in (512, 2048, 4096):
-        X = torch.randn(S, K, device=dev, generator=g).half()
-        Y = torch.empty(S, N, device=dev, dtype=torch.float16)
-        sets = [(X, W, Y) for W in Ws]
-        fn = lambda s, st, S=S: pkg.cuda.linear_f16(  # noqa: E731
-            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), S, N, K, st)
-        ms = time_graph(torch, fn, sets, 10 if S >= 2048 else 20, 3)
-        out[f"prefill_s{S}"] = {"us": ms * 1e3, "tflops": 2.0 * S * N * K / (ms * 1e-3) / 1e12}
-        del X, Y, sets
-    del Ws
-    torch.cuda.empty_cache()
-    # Config 2: the other two decode GEMV shapes (rotating pools > L2)
-    for (N, K, nsets) in ((4096, 4096, 6), (14336, 4096, 4)):
-        sets = [((torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
-                 torch.randn(K, device=dev, generator=g).half(),
-                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
-        fn = lambda s, st, N=N, K=K: pkg.cuda.gemv_f16_nk(  # noqa: E731
-            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), N, K, st)
-        ms = time_graph(torch, fn, sets, 60, 5)
-        byt = 2.0 * (N * K + K + N)
-        out[f"gemv_{N}x{K}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9}
-        del sets
     # Block-quantised decode GEMV (GGUF Q8_0 / Q4_0, the engine's declared formats),
     # 4096x14336, in the streamed layout; random payload bytes and scales (timing
     # only: the same bytes and work as real quantised weights).
@@ -425,12 +437,34 @@ def secondary_configs(torch, pkg, dev, g, world, args):
                  torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
         fn = lambda s, st, qt=qtype: pkg.cuda.gemv_q_nk(  # noqa: E731
             qt, s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), 0, s[3].data_ptr(), N, K, st)
-        ms = time_graph(torch, fn, sets, 60, 5)
         byt = N * pay + 2.0 * (N * K // 32) + 2.0 * (K + N)
-        out[f"gemv_{name}_{N}x{K}"] = {"us": ms * 1e3, "gbs": byt / (ms * 1e-3) / 1e9,
-                                        "bytes_per_launch": byt}
+        timed(f"gemv_{name}_{N}x{K}", fn, sets, 60, 5, byt=byt, extra={"bytes_per_launch": byt})
         del sets
     torch.cuda.empty_cache()
+    # Config 4b: X[S,4096] W[14336,4096]^T
+    N, K = 14336, 4096
+    Ws = [(torch.randn(N, K, device=dev, generator=g) * 0.02).half() for _ in range(2)]
+    for S in (512, 2048, 4096):
+        X = torch.randn(S, K, device=dev, generator=g).half()
+        Y = torch.empty(S, N, device=dev, dtype=torch.float16)
+        sets = [(X, W, Y) for W in Ws]
+        fn = lambda s, st, S=S: pkg.cuda.linear_f16(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), S, N, K, st)
+        timed(f"prefill_s{S}", fn, sets, 10 if S >= 2048 else 20, 3, flops=2.0 * S * N * K)
+        del X, Y, sets
+    del Ws
+    torch.cuda.empty_cache()
+    # The 14336x4096 GEMV again, right after the prefill GEMMs: the same kernel
+    # and weights as the entry at the top of the sequence, so any difference in
+    # "us" or "kcyc" is the GPU's state after long tensor-core work.
+    N, K = 14336, 4096
+    sets = [((torch.randn(N, K, device=dev, generator=g) * 0.02).half(),
+             torch.randn(K, device=dev, generator=g).half(),
+             torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(4)]
+    fn = lambda s, st: pkg.cuda.gemv_f16_nk(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), 0, s[2].data_ptr(), N, K, st)
+    timed("gemv_14336x4096_after_prefill", fn, sets, 60, 5, byt=2.0 * (N * K + K + N))
+    del sets
     # Config 4a in BF16
     n = 4096
     sets = [(torch.randn(n, n, device=dev, generator=g).bfloat16(),
@@ -438,8 +472,7 @@ def secondary_configs(torch, pkg, dev, g, world, args):
              torch.empty(n, n, device=dev, dtype=torch.bfloat16)) for _ in range(4)]
     fn = lambda s, st: pkg.cuda.matmul_bf16(  # noqa: E731
         s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)
-    ms = time_graph(torch, fn, sets, 20, 3)
-    out["matmul_bf16_4096"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
+    timed("matmul_bf16_4096", fn, sets, 20, 3, flops=2.0 * n ** 3)
     del sets
     # Config 1: the reference's FP32 register-tiled matmul at 512^3 (48 rotating
     # 3 MiB sets = 144 MiB > L2)
@@ -449,8 +482,7 @@ def secondary_configs(torch, pkg, dev, g, world, args):
              torch.empty(n, n, device=dev)) for _ in range(48)]
     fn = lambda s, st: pkg.cuda.matmul_register_tiled(  # noqa: E731
         s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)
-    ms = time_graph(torch, fn, sets, 96, 5)
-    out["matmul_f32_512"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
+    timed("matmul_f32_512", fn, sets, 96, 5, flops=2.0 * n ** 3)
     del sets
     # The reference's own headline size for the FP32 register-tiled matmul, 4096^3
     # (2 rotating sets of 192 MiB > L2)
@@ -458,12 +490,108 @@ def secondary_configs(torch, pkg, dev, g, world, args):
     sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
              torch.rand(n, n, device=dev, generator=g) * 2 - 1,
              torch.empty(n, n, device=dev)) for _ in range(2)]
-    ms = time_graph(torch, fn_f32 := (lambda s, st: pkg.cuda.matmul_register_tiled(  # noqa: E731
-        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)), sets, 4, 3)
-    out["matmul_f32_4096"] = {"us": ms * 1e3, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12}
-    del sets, fn_f32
+    fn = lambda s, st: pkg.cuda.matmul_register_tiled(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)
+    timed("matmul_f32_4096", fn, sets, 4, 3, flops=2.0 * n ** 3)
+    del sets
     torch.cuda.empty_cache()
     return with_fractions(out)
+
+
+def old_kernel_baseline(torch, pkg, dev, g):
+    """The reference's own sm_89-design CUDA kernels, compiled unmodified for
+    sm_100a (oracle/_ref/libref_cuda.so), timed beside this library's drop-in on
+    the same GPU, inputs and timing (CUDA graph, operand pools larger than L2):
+    config 1 (FP32 matmul_register_tiled 512^3, and the reference's own 4096^3
+    headline size), the legacy [K,N] gemv_fp16 at 4096x4096 and 4096x14336, and
+    the FP32 rmsnorm_linear dispatcher at one row.  A baseline leg only: nothing
+    of it is in the product path.  None when the library was not built."""
+    orc = _oracle()
+    if not orc.ref_cuda_available():
+        return None
+    ref = orc.ref_cuda_lib()
+    out = {}
+
+    def pair(name, ours, theirs, sets, steps, flops=None, byt=None, graph=True):
+        if graph:
+            ms_o = time_graph(torch, ours, sets, steps, 3, min_ms=20.0)
+            ms_r = time_graph(torch, theirs, sets, steps, 3, min_ms=20.0)
+        else:  # back-to-back eager launches on one stream (the reference's pool
+            # allocator queries events, which a stream capture forbids)
+            st = torch.cuda.current_stream()
+            ms_o = time_launches(torch, lambda x: ours(x, st.cuda_stream), sets, steps, 3, st)[1] / steps
+            ms_r = time_launches(torch, lambda x: theirs(x, st.cuda_stream), sets, steps, 3, st)[1] / steps
+        d = {"ours_us": ms_o * 1e3, "ref_us": ms_r * 1e3, "speedup": ms_r / ms_o,
+             "timing": "cuda graph" if graph else "eager launches"}
+        if flops:
+            d["ours_tflops"] = flops / (ms_o * 1e-3) / 1e12
+            d["ref_tflops"] = flops / (ms_r * 1e-3) / 1e12
+        if byt:
+            d["ours_gbs"] = byt / (ms_o * 1e-3) / 1e9
+            d["ref_gbs"] = byt / (ms_r * 1e-3) / 1e9
+        out[name] = d
+
+    def chk(rc):
+        if rc != 0:
+            raise RuntimeError("reference CUDA launcher failed")
+
+    for n, nsets, steps in ((512, 48, 96), (4096, 2, 4)):
+        sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.empty(n, n, device=dev)) for _ in range(nsets)]
+        pair(f"matmul_register_tiled_f32_{n}",
+             lambda s, st, n=n: pkg.cuda.matmul_register_tiled(
+                 s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st),
+             lambda s, st, n=n: chk(ref.refcuda_matmul_register_tiled(
+                 s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)),
+             sets, steps, flops=2.0 * n ** 3)
+        del sets
+    for (N, K, nsets) in ((4096, 4096, 6), (4096, 14336, 4)):  # legacy A[K,N]
+        sets = [((torch.randn(K, N, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        pair(f"gemv_fp16_kn_{K}x{N}",
+             lambda s, st, N=N, K=K: pkg.cuda.gemv_fp16(
+                 s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), N, K, st),
+             lambda s, st, N=N, K=K: chk(ref.refcuda_gemv_fp16(
+                 s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), N, K, st)),
+             sets, 40, byt=2.0 * (N * K + K + N))
+        del sets
+    N = K = 4096  # FP32 rmsnorm_linear, one row (the reference dispatches rmsnorm + gemv)
+    sets = [(torch.randn(1, K, device=dev, generator=g), 1 + 0.1 * torch.randn(K, device=dev, generator=g),
+             torch.randn(K, N, device=dev, generator=g) * 0.02,
+             torch.empty(1, N, device=dev)) for _ in range(3)]
+    pair("rmsnorm_linear_f32_1x4096x4096",
+         lambda s, st: pkg.cuda.rmsnorm_linear(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),
+                                               s[3].data_ptr(), 1, N, K, 1e-5, st),
+         lambda s, st: chk(ref.refcuda_rmsnorm_linear(s[0].data_ptr(), s[1].data_ptr(),
+                                                      s[2].data_ptr(), s[3].data_ptr(), 1, N, K,
+                                                      1e-5, st)),
+         sets, 40, byt=4.0 * (N * K + 2 * K + N), graph=False)
+    del sets
+    torch.cuda.empty_cache()
+    out["note"] = ("the reference's kernels/*.cu compiled unmodified for sm_100a; same inputs "
+                   "and timing for both; speedup = ref_us / ours_us")
+    return out
+
+
+def _sig(x, n: int = 4):
+    """x rounded to n significant digits (floats only)."""
+    if isinstance(x, bool) or not isinstance(x, float) or x == 0.0 or x != x:
+        return x
+    return float(f"{x:.{n}g}")
+
+
+def compact(d):
+    """A nested result with every float rounded to 4 significant digits, so the
+    JSON line stays short enough for a log tail to hold its last blocks."""
+    if d is None:
+        return None
+    if isinstance(d, dict):
+        return {k: compact(v) for k, v in d.items()}
+    if isinstance(d, (list, tuple)):
+        return [compact(v) for v in d]
+    return _sig(d)
 
 
 # FP32 SIMT peak for the CUDA-core GEMMs: 148 SMs x 128 FMA/clk x 2 FLOP x 1.965 GHz
@@ -478,12 +606,92 @@ def with_fractions(out: dict) -> dict:
     pk, kind = peaks()
     for name, d in out.items():
         if "gbs" in d:
-            d["frac"], d["peak_kind"] = d["gbs"] / pk["hbm_gbs"], f"{kind} HBM copy"
+            d["frac"] = d["gbs"] / pk["hbm_gbs"]
         elif name.startswith("matmul_f32"):
-            d["frac"], d["peak_kind"] = d["tflops"] / FP32_SIMT_TFLOPS, "nominal FP32 SIMT"
+            d["frac"] = d["tflops"] / FP32_SIMT_TFLOPS
         elif "tflops" in d:
-            d["frac"], d["peak_kind"] = d["tflops"] / pk["bf16_tflops"], f"{kind} bf16 dense burst"
+            d["frac"] = d["tflops"] / pk["bf16_tflops"]
+    out["peaks"] = {"gbs": f"{kind} HBM copy {pk['hbm_gbs']}",
+                    "tflops": f"{kind} bf16 dense burst {pk['bf16_tflops']}",
+                    "matmul_f32": f"nominal FP32 SIMT {FP32_SIMT_TFLOPS:.1f}"}
     return out
+
+
+def e2e_pipelined(torch, pkg, dev, n: int, steps: int, warmup: int, world: int):
+    """The headline GEMM end to end through the C ABI with pinned HOST buffers:
+    every step copies its A and B host->device, runs engine_cuda_matmul_f16 and
+    reads C back.  Steps are pipelined over three streams and two device buffer
+    sets -- the H2D copies of step i+1 and the D2H copy of step i-1 run on the two
+    copy engines while step i computes -- with events ordering each buffer's
+    reuse.  Returns (ms for `steps` steps, max over ranks, H2D and D2H bytes per
+    step)."""
+    g = torch.Generator().manual_seed(1)
+    hA = torch.randn(n, n, generator=g).half().pin_memory()
+    hB = torch.randn(n, n, generator=g).half().pin_memory()
+    hC = [torch.empty(n, n, dtype=torch.float16).pin_memory() for _ in range(2)]
+    dA = [torch.empty(n, n, device=dev, dtype=torch.float16) for _ in range(2)]
+    dB = [torch.empty_like(dA[0]) for _ in range(2)]
+    dC = [torch.empty_like(dA[0]) for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+
+    def run(k: int):
+        loaded = [None, None]      # H2D of the step that last used buffer set j finished
+        computed = [None, None]    # its GEMM finished (A, B free again)
+        read = [None, None]        # its D2H finished (C free again)
+        for i in range(k):
+            j = i & 1
+            with torch.cuda.stream(h2d):
+                if computed[j] is not None:
+                    h2d.wait_event(computed[j])
+                dA[j].copy_(hA, non_blocking=True)
+                dB[j].copy_(hB, non_blocking=True)
+                loaded[j] = ev()
+                loaded[j].record(h2d)
+            comp.wait_event(loaded[j])
+            if read[j] is not None:
+                comp.wait_event(read[j])
+            pkg.cuda.matmul_f16(dA[j].data_ptr(), dB[j].data_ptr(), dC[j].data_ptr(), n, n, n,
+                                comp.cuda_stream)
+            computed[j] = ev()
+            computed[j].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(computed[j])
+                hC[j].copy_(dC[j], non_blocking=True)
+                read[j] = ev()
+                read[j].record(d2h)
+        for r in read:
+            if r is not None:
+                comp.wait_event(r)
+
+    run(warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    run(steps)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    return ms, 2 * n * n * 2, n * n * 2
+
+
+def sustained_gemm(torch, gemm, sets, seconds: float, stream, local: int):
+    """Back-to-back launches for about `seconds` of device time (under the
+    power cap); returns (ms per launch, launches, clock summary)."""
+    per, _ = time_launches(torch, gemm, sets, 20, 3, stream)
+    count = max(50, int(seconds * 1e3 / max(statistics.mean(per), 1e-3)))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local, period_s=0.01) as clk:
+        e0.record(stream)
+        for i in range(count):
+            gemm(sets[i % len(sets)])
+        e1.record(stream)
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / count, count, clk.summary()
 
 
 def run_headline(args):
@@ -518,15 +726,29 @@ def run_headline(args):
                                          n, n, n, sp)
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, period_s=0.001) as clk:
         per, total_ms = time_launches(torch, gemm, sets, args.steps, args.warmup, stream)
     barrier(world)
     flops = 2.0 * n * n * n
     total_ms_max = max_over_ranks(total_ms, world)
     value = world * flops * args.steps / (total_ms_max * 1e-3) / 1e12
-    gemm_kernel_ms = statistics.mean(per)
+
+    # ---- roofline: a dedicated loop of >= 400 launches (per-launch CUDA events,
+    # clocks sampled), independent of --steps; then the same GEMM as one CUDA
+    # graph of back-to-back launches beside cuBLAS (torch.mm, not the product
+    # path) on the same operands, and ~1.5 s of launches under the power cap.
+    rsteps = max(400, args.steps)
+    with ClockSampler(local, period_s=0.002) as rclk:
+        rper, _ = time_launches(torch, gemm, sets, rsteps, 3, stream)
+    gemm_kernel_ms = statistics.mean(rper)
     achieved = flops / (gemm_kernel_ms * 1e-3) / 1e12
     peak_t = pk["bf16_tflops"]
+    ours_graph = time_graph(torch, lambda s, st: pkg.cuda.matmul_f16(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st), sets, 40, 3, reps=7)
+    cublas_graph = time_graph(torch, lambda s, st: torch.mm(s[0], s[1], out=s[2]),  # noqa: E731
+                              sets, 40, 3, reps=7)
+    sus_ms, sus_count, sus_clk = sustained_gemm(torch, gemm, sets, 1.5, stream, local)
+    sus_tf = flops / (sus_ms * 1e-3) / 1e12
     del sets
     torch.cuda.empty_cache()
 
@@ -542,7 +764,9 @@ def run_headline(args):
                                               s[2].data_ptr(), Nv, Kv, st)
     gsteps = max(args.steps, 50)
     barrier(world)
-    gst = time_graph(torch, gemv, wsets, gsteps, max(args.warmup, 3), reps=7, stats=True)
+    with ClockSampler(local, period_s=0.001) as gclk:
+        gst = time_graph(torch, gemv, wsets, gsteps, max(args.warmup, 3), reps=7, stats=True,
+                         min_ms=40.0)
     gemv_kernel_ms = max_over_ranks(gst["median"], world)
     gbytes = 2.0 * (Nv * Kv + Kv + Nv)
     gemv_gbs = gbytes / (gemv_kernel_ms * 1e-3) / 1e9
@@ -550,36 +774,28 @@ def run_headline(args):
     del wsets
     torch.cuda.empty_cache()
 
-    secondary = secondary_configs(torch, pkg, dev, g, world, args) if not args.skip_secondary else None
+    secondary = (secondary_configs(torch, pkg, dev, g, world, args, local)
+                 if not args.skip_secondary else None)
 
-    # ---- e2e through the C ABI with pinned host buffers
-    hA = torch.randn(n, n, generator=torch.Generator().manual_seed(1)).half().pin_memory()
-    hB = torch.randn(n, n, generator=torch.Generator().manual_seed(2)).half().pin_memory()
-    hC = torch.empty(n, n, dtype=torch.float16).pin_memory()
-    dA = torch.empty(n, n, device=dev, dtype=torch.float16)
-    dB = torch.empty_like(dA)
-    dC = torch.empty_like(dA)
+    # ---- e2e through the C ABI with pinned host buffers (copies pipelined)
     esteps = max(3, min(args.steps, 50))
-
-    def e2e_step():
-        dA.copy_(hA, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
-        pkg.cuda.matmul_f16(dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), n, n, n, sp)
-        hC.copy_(dC, non_blocking=True)
-
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(esteps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_ms, h2d_b, d2h_b = e2e_pipelined(torch, pkg, dev, n, esteps, max(args.warmup, 3), world)
     e2e_value = world * flops * esteps / (e2e_ms * 1e-3) / 1e12
+    torch.cuda.empty_cache()
+
+    # ---- the reference's own CUDA kernels on this GPU (baseline leg, rank 0 of N=1)
+    old = None
+    if world == 1 and not args.skip_secondary:
+        old = old_kernel_baseline(torch, pkg, dev, g)
+
+    # ---- tensor-parallel layer set at t = world (every rank)
+    tpb = None
+    if not args.skip_tp:
+        from bmle_b200 import tp as _tp
+
+        tpb = _tp.bench_tp_block(args.steps, min(args.warmup, 3), pk["hbm_gbs"],
+                                 pk["bf16_tflops_sustained"],
+                                 f"{pk_kind} HBM copy (decode) / {pk_kind} bf16 sustained (prefill)")
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
@@ -599,36 +815,47 @@ def run_headline(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,1) FP16 operands (torch Philox), W ~ N(0,0.02)",
-        "config": dict(headline_config(world),
-                       l2="rotating operand pools larger than the 126 MB L2 "
-                          "(4 x 96 MiB GEMM sets, 4 x 112 MiB GEMV weights)"),
+        "config": headline_config(world),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": achieved / peak_t, "traffic": traffic,
                      "peak_kind": f"{pk_kind} bf16 dense burst",
                      "kernel": "gemm_tc2_kernel<256> 4096^3 (2-SM tcgen05, 256x256 tiles, stream-K tail)",
-                     "kernel_ms": gemm_kernel_ms,
-                     "kernel_ms_median": statistics.median(per),
-                     "kernel_ms_iqr": (lambda q: [q[0], q[2]])(statistics.quantiles(per, n=4))
-                     if len(per) > 1 else None},
+                     "kernel_ms": gemm_kernel_ms, "launches": rsteps,
+                     "kernel_ms_median": statistics.median(rper),
+                     "kernel_ms_iqr": (lambda q: [q[0], q[2]])(statistics.quantiles(rper, n=4)),
+                     "clocks": rclk.summary(),
+                     "graph_kernel_ms": ours_graph,
+                     "cublas_ref_graph_ms": cublas_graph,
+                     "sustained": {"kernel_ms": sus_ms, "launches": sus_count,
+                                   "achieved": sus_tf, "peak": pk["bf16_tflops_sustained"],
+                                   "frac": sus_tf / pk["bf16_tflops_sustained"],
+                                   "peak_kind": f"{pk_kind} bf16 dense sustained",
+                                   "clocks": sus_clk}},
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_b,
+                "d2h_bytes_per_step": d2h_b,
+                "pipeline": "H2D of step i+1 and D2H of step i-1 overlap step i's GEMM "
+                            "(three streams, two buffer sets)"},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "environment": environment(with_gpu=True),
+        "other_configs": compact(secondary),
+        "old_kernel_baseline": compact(old),
+        "tp": compact(tpb),
         "gemv": {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / pk["hbm_gbs"],
                  "peak": pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy",
                  "kernel_us": gemv_kernel_ms * 1e3, "job_gbs": gemv_job,
                  "kernel_us_iqr": [gst["q1"] * 1e3, gst["q3"] * 1e3],
                  "bytes_per_launch": gbytes, "traffic": traffic_for("gemv_nk_4096x14336"),
+                 "mhz": gclk.median(),
                  "timing": "CUDA graph of back-to-back launches, 4 x 112 MiB rotating weights"},
-        "other_configs": secondary,
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2},
-        "cpu_baseline": cpu,
-        "gpu_launches": args.steps,
-        "clocks": clk.summary(),
-        "environment": environment(with_gpu=True),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
@@ -731,6 +958,8 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-secondary", action="store_true")
+    ap.add_argument("--skip-tp", action="store_true",
+                    help="leave out the tensor-parallel layer-set block of the headline line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -24,10 +24,20 @@
  *
  * All calls are asynchronous and stream-ordered and safe to call from several
  * host threads on different streams.  Split-K partial sums are reduced through
- * distributed shared memory inside a thread-block cluster, so the GEMM and GEMV
- * paths need no scratch; the one exception is engine_cuda_rmsnorm_linear_f16
- * with M > 4, whose normalised activation rows come from a library-owned
- * stream-ordered memory pool.
+ * distributed shared memory inside a thread-block cluster, so the GEMV paths and
+ * the small-batch projections need no scratch.  Device memory the library
+ * allocates itself:
+ *   - from a library-owned stream-ordered memory pool (cached between calls):
+ *     engine_cuda_rmsnorm_linear_f16 with M > 4 (normalised activation rows),
+ *     engine_cuda_rmsnorm_linear_swiglu_f16 with M > 1 (the gate/up rows) and
+ *     engine_cuda_attention_decode / _prefill with more than one KV split (the
+ *     split partials);
+ *   - once per (device, stream), on the first call that needs it, never during
+ *     a stream capture: the stream-K workspace of the large 16-bit GEMMs
+ *     (engine_cuda_matmul_* / linear_* with M, N >= 256; about 38 MB);
+ *   - at engine_tp_comm_create: the communicator's exchange region.
+ * engine_cuda_rmsnorm_linear_f16_noalloc is the variant of the fused norm
+ * projection that allocates nothing.
  *
  * FP16 / BF16 data crosses the ABI as 16-bit IEEE binary16 / bfloat16 bit
  * patterns (engine::half is __half: the same 2-byte layout, half.hpp:28).
@@ -165,16 +175,21 @@ ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16(const engine_half_t* x, const
                                    float eps, engine_stream_t stream);
 
 /* rmsnorm_linear_f16 for callers that cannot allocate device memory.  No
- * counterpart in the reference.  Same arguments and result as
+ * counterpart in the reference.  Same arguments as
  * engine_cuda_rmsnorm_linear_f16, but the normalised activations live in a
  * fixed 2 MiB array inside the library instead of a stream-ordered pool, so the
  * call allocates nothing: for serving loops that reserve all device memory at
  * start-up and may not allocate per request, and for hosts whose device memory
- * is owned by another allocator.  Limits: 1 <= M <= 32, K <= 16384, K a multiple
- * of 8, W 16-byte aligned; larger sizes return ENGINE_ERR_UNSUPPORTED.  The
- * first call on each device looks up the array's device address; make it before
- * any stream capture.  All calls share the one array: calls that overlap on the
- * GPU race. */
+ * is owned by another allocator.  It always takes the tensor-core path with
+ * hi/lo activations: for 5 <= M <= 32 the result is identical to
+ * engine_cuda_rmsnorm_linear_f16's; for M <= 4, where that entry point uses the
+ * CUDA-core GEMV, the two agree within rounding (both inside the FP32 bound).
+ * Limits: 1 <= M <= 32, K <= 16384, K a multiple of 8, W 16-byte aligned;
+ * larger sizes return ENGINE_ERR_UNSUPPORTED.  Make one warm-up call per device
+ * at start-up: it looks up the array's device address, and with lazy module
+ * loading it is also the call that loads the library's device code, which is
+ * when the 2 MiB array is reserved.  Make it before any stream capture.  All
+ * calls share the one array: calls that overlap on the GPU race. */
 ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16_noalloc(
     const engine_half_t* x, const engine_half_t* gamma, const engine_half_t* W,
     const engine_half_t* residual, engine_half_t* Y, int64_t M, int64_t N, int64_t K, float eps,

@@ -9,9 +9,16 @@ arrays:
 * ``_ref/libref_cpu.so`` -- the reference's OWN ``src/cpu_ref`` sources compiled
   in place by ``oracle/Makefile`` (present only where the reference tree was
   available when ``build()`` ran; it travels to the GPU box as a built file).
+* ``_ref/libref_cuda.so`` -- the reference's own CUDA launchers compiled for
+  sm_100a: bench.py's same-GPU "old kernel" baseline leg.
 
-Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline /
-reference arm may import this package.  The CUDA library never does.
+The reference tree is found by ``reference_dir()``: the ENGINE_REF_DIR
+environment variable, else a checkout named ``reference`` beside this
+repository.
+
+Only ``tests/``, ``__graft_entry__`` and ``bench.py``'s baseline legs (the CPU
+baseline, the old-kernel baseline and the reference arm) may import this
+package.  The CUDA library never does.
 """
 from __future__ import annotations
 
@@ -25,6 +32,17 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 _LIB = HERE / "liboracle.so"
 _REF = HERE / "_ref" / "libref_cpu.so"
+_REF_CUDA = HERE / "_ref" / "libref_cuda.so"
+
+
+def reference_dir():
+    """The reference engine's source tree, or None: ENGINE_REF_DIR when set,
+    else a checkout named ``reference`` beside this repository (it must hold
+    src/cpu_ref).  Only build steps and fixture generators read it; nothing that
+    runs on a GPU box does."""
+    env = os.environ.get("ENGINE_REF_DIR")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "src" / "cpu_ref").is_dir() else None
 
 _i64 = ctypes.c_int64
 _p = ctypes.c_void_p
@@ -118,6 +136,35 @@ def ref_lib():
             fn.argtypes = args
         _ref = r
     return _ref
+
+
+_refcuda = None
+
+
+def ref_cuda_available() -> bool:
+    return _REF_CUDA.exists()
+
+
+def ref_cuda_lib():
+    """The reference's own CUDA launchers built for sm_100a (raises if never built)."""
+    global _refcuda
+    if _refcuda is None:
+        if not _REF_CUDA.exists():
+            raise FileNotFoundError(f"{_REF_CUDA} not built (make -C oracle refcuda)")
+        r = ctypes.CDLL(str(_REF_CUDA))
+        sig = {
+            "refcuda_matmul_register_tiled": [_p, _p, _p, _i64, _i64, _i64, _p],
+            "refcuda_matmul_tiled": [_p, _p, _p, _i64, _i64, _i64, _p],
+            "refcuda_gemv": [_p, _p, _p, _i64, _i64, _p],
+            "refcuda_gemv_fp16": [_p, _p, _p, _i64, _i64, _p],
+            "refcuda_rmsnorm_linear": [_p, _p, _p, _p, _i64, _i64, _i64, _f, _p],
+        }
+        for name, args in sig.items():
+            fn = getattr(r, name)
+            fn.restype = _i
+            fn.argtypes = args
+        _refcuda = r
+    return _refcuda
 
 
 def ncores() -> int:

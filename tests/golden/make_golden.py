@@ -28,6 +28,7 @@ import argparse
 import hashlib
 import importlib.util
 import json
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -45,8 +46,18 @@ def sha(a: np.ndarray) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None,
+                    help="the reference source tree (default: ENGINE_REF_DIR, else a "
+                         "`reference` checkout beside this repository)")
     args = ap.parse_args()
+    if args.reference is None:
+        sys.path.insert(0, str(HERE.parent.parent))
+        import oracle
+
+        ref = oracle.reference_dir()
+        if ref is None:
+            raise SystemExit("reference tree not found: pass --reference or set ENGINE_REF_DIR")
+        args.reference = str(ref)
 
     gen_path = Path(args.reference) / "tools" / "gen_reference.py"
     spec = importlib.util.spec_from_file_location("ref_gen_reference", gen_path)

@@ -54,9 +54,9 @@ def test_warmup_is_at_least_three():
 
 
 def test_secondary_lines_carry_their_roofline_fraction():
-    """Every other_configs line gets frac and peak_kind: HBM lines against the
-    measured copy bandwidth, tensor lines against the bf16 burst peak, FP32
-    CUDA-core lines against the nominal SIMT peak."""
+    """Every other_configs line gets frac: HBM lines against the measured copy
+    bandwidth, tensor lines against the bf16 burst peak, FP32 CUDA-core lines
+    against the nominal SIMT peak; one "peaks" entry names the three peaks."""
     import importlib.util
     spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
     b = importlib.util.module_from_spec(spec)
@@ -68,4 +68,29 @@ def test_secondary_lines_carry_their_roofline_fraction():
     assert out["gemv_4096x4096"]["frac"] == 4800.0 / pk["hbm_gbs"]
     assert out["prefill_s2048"]["frac"] == 1320.0 / pk["bf16_tflops"]
     assert abs(out["matmul_f32_512"]["frac"] - 18.3 / 74.4) < 1e-3
-    assert all("peak_kind" in d for d in out.values())
+    assert set(out["peaks"]) == {"gbs", "tflops", "matmul_f32"}
+    assert all("frac" in d for k, d in out.items() if k != "peaks")
+
+
+def test_compact_rounds_floats_and_keeps_structure():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    d = b.compact({"a": {"us": 11.623680591583252, "n": 3, "ok": True, "s": "x"},
+                   "l": [0.1234567, None]})
+    assert d == {"a": {"us": 11.62, "n": 3, "ok": True, "s": "x"}, "l": [0.1235, None]}
+    assert b.compact(None) is None
+
+
+def test_reference_arm_config_equals_ours():
+    """Both arms quote the same config dict, so the driver compares like with like."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", ROOT / "bench.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                        "--steps", "1", "--warmup", "3"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    d = json.loads([ln for ln in r.stdout.splitlines() if ln.strip().startswith("{")][0])
+    assert d["config"] == b.headline_config(1)

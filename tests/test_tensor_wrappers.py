@@ -17,12 +17,15 @@ import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 BIN = ROOT / "oracle" / "_ref" / "tensor_wrappers_test"
-REFERENCE = Path("/root/reference/src/tensor.cpp")
 
 
 def _binary(rebuild: bool) -> Path:
-    if rebuild and REFERENCE.exists():  # the CPU test rebuilds when sources changed
-        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "tensor"], check=True)
+    import oracle
+
+    ref = oracle.reference_dir()
+    if rebuild and ref is not None:  # the CPU test rebuilds when sources changed
+        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), f"REF={ref}", "tensor"],
+                       check=True)
     if not BIN.exists():
         pytest.skip("oracle/_ref/tensor_wrappers_test not built (needs the reference tree)")
     return BIN

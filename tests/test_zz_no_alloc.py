@@ -13,6 +13,11 @@ already run every other test.
 """
 from __future__ import annotations
 
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -90,3 +95,40 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(pkg, dev):
     with pytest.raises(pkg.EngineError):
         pkg.cuda.rmsnorm_linear_f16_noalloc(t["x"].data_ptr(), t["g"].data_ptr(), t["W"].data_ptr(),
                                             0, Y.data_ptr(), 1, 64, 16392, EPS)
+
+
+def test_noalloc_reserves_no_device_memory_per_call(pkg, dev):
+    """The property the entry point exists for.  In a fresh process (so no pool
+    of the library holds cached blocks from earlier calls): one warm-up call,
+    then calls at the largest and smaller sizes; the device's free memory
+    (cudaMemGetInfo) must not move.  A variant that drew on the library's
+    stream-ordered pool would reserve at least its 2 MiB of activation rows."""
+    root = Path(__file__).resolve().parent.parent
+    code = textwrap.dedent(f"""
+        import sys
+        sys.path.insert(0, {str(root)!r})
+        import torch
+        from tests.conftest import load_package
+        pkg = load_package()
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        K, N = 16384, 256
+        x = torch.randn(32, K, device=dev).half()
+        g = torch.ones(K, device=dev).half()
+        W = (torch.randn(N, K, device=dev) * 0.02).half()
+        Y = torch.empty(32, N, device=dev, dtype=torch.float16)
+        f = pkg.cuda.rmsnorm_linear_f16_noalloc
+        f(x.data_ptr(), g.data_ptr(), W.data_ptr(), 0, Y.data_ptr(), 32, N, K, 1e-5)
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for M in (32, 7, 1, 32, 16):
+            f(x.data_ptr(), g.data_ptr(), W.data_ptr(), 0, Y.data_ptr(), M, N, K, 1e-5)
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        print("FREE", free0, free1)
+    """)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("FREE")][0]
+    free0, free1 = map(int, line.split()[1:])
+    assert free1 == free0, f"free device memory moved by {free0 - free1} bytes"
