@@ -130,6 +130,12 @@ using TmapKey = std::tuple<int, const void*, int, uint64_t, uint64_t, uint64_t, 
 std::map<TmapKey, CUtensorMap> g_tmaps;
 }  // namespace
 
+// L2 sector promotion of the 2-D tensor maps (CUtensorMapL2promotion: 0 none,
+// 1 64B, 2 128B, 3 256B), a compile-time tunable.
+#ifndef ENGINE_TMAP_L2_PROMOTION
+#define ENGINE_TMAP_L2_PROMOTION 3
+#endif
+
 bool make_tmap_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
                   uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                   uint32_t box_cols) {
@@ -157,7 +163,8 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, 
   std::memset(&m, 0, sizeof(m));
   const CUresult r = enc(&m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         static_cast<CUtensorMapL2promotion>(ENGINE_TMAP_L2_PROMOTION),
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error(ENGINE_ERR_UNSUPPORTED,
               "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +
@@ -170,6 +177,32 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, 
     g_tmaps.emplace(key, m);
   }
   *out = m;
+  return true;
+}
+
+bool make_tmap_3d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+                  const uint32_t (&box)[3]) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (enc == nullptr) {
+    set_error(ENGINE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    return false;
+  }
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t st[2] = {strides[0] * static_cast<uint64_t>(elem_bytes),
+                            strides[1] * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t b[3] = {box[0], box[1], box[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  std::memset(out, 0, sizeof(*out));
+  const CUresult r = enc(out, dtype, 3, const_cast<void*>(ptr), d, st, b, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(ENGINE_ERR_UNSUPPORTED,
+              "cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string(static_cast<int>(r)) +
+                  "): pointer/stride not 16-byte aligned or box too large");
+    return false;
+  }
   return true;
 }
 

@@ -20,7 +20,9 @@
 // Decode (one query position) gets enough splits to fill the GPU.  Prefill runs
 // the same kernel per query position: a correctness baseline for the engine's
 // prefill API; the tensor-core FlashAttention-2 prefill is the next step.
+#include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -30,6 +32,15 @@ namespace b200 {
 namespace {
 
 constexpr int kAttnWarps = 4;
+// attention_prefill takes the tcgen05 kernel from this many query rows up; below
+// it, the split kernel's per-position CTAs fill the GPU better.
+constexpr int64_t kAttnTcMinRows = 16;
+
+int env_flag(const char* name, int dflt) {
+  const char* e = std::getenv(name);
+  if (e == nullptr || e[0] == '\0') return dflt;
+  return static_cast<int>(std::strtol(e, nullptr, 10));
+}
 constexpr int kAttnUnroll = 4;  // keys per lane group per step (loads issued first)
 
 template <bool VEC>
@@ -213,6 +224,271 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- decode (bulk)
+//
+// attention_decode with K / V streamed by bulk copies.  The keys of one KV head
+// are contiguous ([n_kv_heads][kv_head_stride], key j at j * d), so a CTA's
+// split arrives as whole 64-key blocks of K and of V, each ONE cp.async.bulk
+// into a two-stage shared-memory ring: all of a block's bytes are in flight at
+// once.  Per block the CTA (4 warps, GB query heads of one KV group) forms the
+// scores (lane groups of d/8 lanes per key, shuffle-reduced), the block max and
+// probabilities per head, and O = alpha * O + P V with one thread per output
+// pair of elements -- one rescale per 64 keys, not per key.  The split's
+// (m, l, O) goes to the workspace for attn_merge_kernel (split order), or with
+// one split straight to out.  Scores use the natural base (expf), like the
+// split kernel, so the two share the merge.
+constexpr int kDecBlock = 64;  // keys per bulk block
+
+constexpr int kDecWarps = 8;
+template <int D, int GB>
+struct DecCfg {
+  static constexpr int kBlockBytes = kDecBlock * D * 2;  // one block of K (or V)
+  static constexpr int kRing = 2;                        // stages at most
+  /// Dynamic shared memory for `stages` ring stages plus the barriers.
+  static constexpr int smem(int stages) { return stages * 2 * kBlockBytes + 64; }
+};
+
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int D, int GB, bool FINAL>
+__global__ void __launch_bounds__(kDecWarps * 32)
+    attn_decode_bulk_kernel(const AttnArgs a, int nst, unsigned int* err,
+                            unsigned long long limit_ns) {
+  using Cfg = DecCfg<D, GB>;
+  constexpr int LPK = D / 8;                 // lanes per key row
+  constexpr int KPW = 32 / LPK;              // key rows per warp per step
+  constexpr int NP = D / 2;                  // element pairs per head
+  constexpr int GS = (kDecWarps * 32) / NP;  // heads one pass of the threads covers
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint8_t* ring = dsm;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + nst * 2 * Cfg::kBlockBytes);
+  __shared__ float s_p[GB][kDecBlock];
+  __shared__ float s_m[GB], s_l[GB], s_alpha[GB];
+  __shared__ int s_ok;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane % LPK, kgw = lane / LPK;
+  const int64_t group = a.n_heads / a.n_kv_heads;
+  const int64_t chunks_per_kv = group / GB;
+  const int64_t h_kv = blockIdx.y / chunks_per_kv;
+  const int64_t h0 = h_kv * group + (blockIdx.y % chunks_per_kv) * GB;
+  const int split = blockIdx.x;
+  const int64_t j0 = static_cast<int64_t>(split) * a.chunk;
+  int64_t j1 = j0 + a.chunk;
+  if (j1 > a.s_kv) j1 = a.s_kv;
+  const int nblk = j1 > j0 ? static_cast<int>((j1 - j0 + kDecBlock - 1) / kDecBlock) : 0;
+  const __half* kh = a.k + h_kv * a.kv_head_stride;
+  const __half* vh = a.v + h_kv * a.kv_head_stride;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+    s_ok = 1;
+  }
+  if (threadIdx.x < GB) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.0f;
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  // Block b of the split goes to stage b % nst; the use of a stage's barrier
+  // by block b is its (b / nst)-th phase.
+  auto issue = [&](int b) {  // thread 0
+    const int64_t jb = j0 + static_cast<int64_t>(b) * kDecBlock;
+    const int64_t n = (j1 - jb < kDecBlock) ? j1 - jb : kDecBlock;
+    const uint32_t bytes = static_cast<uint32_t>(n * D * 2);
+    uint8_t* st = ring + (b % nst) * 2 * Cfg::kBlockBytes;
+    mbar_arrive_expect_tx(&full[b % nst], 2 * bytes);
+    bulk_load_1d(st, kh + jb * D, bytes, &full[b % nst]);
+    bulk_load_1d(st + Cfg::kBlockBytes, vh + jb * D, bytes, &full[b % nst]);
+  };
+  int issued = 0;
+  if (threadIdx.x == 0) {
+    for (; issued < nblk && issued < nst; ++issued) issue(issued);
+  }
+
+  float qf[GB][8];
+#pragma unroll
+  for (int g = 0; g < GB; ++g) {
+    load8<true>(a.q + (h0 + g) * D + 8 * sub, qf[g]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qf[g][e] *= a.scale;
+  }
+  const int pr = threadIdx.x % NP;  // this thread's element pair of O
+  const int gs = threadIdx.x / NP;  // its heads: gs, gs + GS, ...
+  float o0[GB], o1[GB];
+#pragma unroll
+  for (int g = 0; g < GB; ++g) o0[g] = o1[g] = 0.0f;
+
+  int consumed = 0;
+  for (int b = 0; b < nblk; ++b) {
+    if (!mbar_wait(&full[b % nst], (b / nst) & 1u, limit_ns, err)) s_ok = 0;
+    __syncthreads();
+    if (!s_ok) break;
+    consumed = b + 1;
+    const uint8_t* st = ring + (b % nst) * 2 * Cfg::kBlockBytes;
+    const __half* ks = reinterpret_cast<const __half*>(st);
+    const __half* vs = reinterpret_cast<const __half*>(st + Cfg::kBlockBytes);
+    const int64_t jb = j0 + static_cast<int64_t>(b) * kDecBlock;
+    const int n = static_cast<int>((j1 - jb < kDecBlock) ? j1 - jb : kDecBlock);
+    // scores: each lane group takes one key per step
+    for (int kb = warp * KPW; kb < kDecBlock; kb += kDecWarps * KPW) {
+      const int kk = kb + kgw;
+      const bool valid = kk < n;
+      float kf[8];
+      if (valid) {
+        const uint4 u = *reinterpret_cast<const uint4*>(ks + kk * D + 8 * sub);
+        const __half2* hh = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __half22float2(hh[i]);
+          kf[2 * i] = t.x;
+          kf[2 * i + 1] = t.y;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GB; ++g) {
+        float sc = 0.0f;
+        if (valid) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sc = fmaf(qf[g][e], kf[e], sc);
+        }
+#pragma unroll
+        for (int off = LPK / 2; off > 0; off >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        if (sub == 0) s_p[g][kk] = valid ? sc : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // per head (warp w takes heads w, w + 4, ...): block max, probabilities, running (m, l)
+    for (int g = warp; g < GB; g += kDecWarps) {
+      float mx = -INFINITY;
+      for (int t = lane; t < kDecBlock; t += 32) mx = fmaxf(mx, s_p[g][t]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = s_m[g];
+      const float m_new = fmaxf(m_old, mx);
+      float sum = 0.0f;
+      for (int t = lane; t < kDecBlock; t += 32) {
+        const float pv = (t < n) ? expf(s_p[g][t] - m_new) : 0.0f;
+        s_p[g][t] = pv;
+        sum += pv;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      __syncwarp();
+      if (lane == 0) {
+        const float al = expf(m_old - m_new);  // m_old = -inf: 0
+        s_alpha[g] = al;
+        s_l[g] = s_l[g] * al + sum;
+        s_m[g] = m_new;
+      }
+    }
+    __syncthreads();
+    // O = alpha O + P V
+#pragma unroll
+    for (int g = 0; g < GB; ++g) {
+      if (g % GS != gs) continue;
+      const float al = s_alpha[g];
+      // two interleaved chains per element (even / odd keys), added at the end
+      float a0 = 0.0f, a1 = 0.0f, c0 = 0.0f, c1 = 0.0f;
+      int t = 0;
+#pragma unroll 4
+      for (; t + 1 < n; t += 2) {
+        const float p0 = s_p[g][t], p1 = s_p[g][t + 1];
+        const float2 v0 = __half22float2(reinterpret_cast<const __half2*>(vs + t * D)[pr]);
+        const float2 v1 = __half22float2(reinterpret_cast<const __half2*>(vs + (t + 1) * D)[pr]);
+        a0 = fmaf(p0, v0.x, a0);
+        a1 = fmaf(p0, v0.y, a1);
+        c0 = fmaf(p1, v1.x, c0);
+        c1 = fmaf(p1, v1.y, c1);
+      }
+      if (t < n) {
+        const float p0 = s_p[g][t];
+        const float2 v0 = __half22float2(reinterpret_cast<const __half2*>(vs + t * D)[pr]);
+        a0 = fmaf(p0, v0.x, a0);
+        a1 = fmaf(p0, v0.y, a1);
+      }
+      o0[g] = o0[g] * al + (a0 + c0);
+      o1[g] = o1[g] * al + (a1 + c1);
+    }
+    __syncthreads();  // stage b and s_p fully read: refill
+    if (threadIdx.x == 0 && issued < nblk) {
+      issue(issued);
+      ++issued;
+    }
+  }
+  // No copy may be writing shared memory when the CTA leaves (only after a
+  // time-out are issued blocks left unconsumed): wait for them, bounded.
+  if (threadIdx.x == 0) {
+    for (int b = consumed; b < issued; ++b) mbar_wait(&full[b % nst], (b / nst) & 1u, limit_ns, err);
+  }
+  if (!s_ok) return;
+#pragma unroll
+  for (int g = 0; g < GB; ++g) {
+    if (g % GS != gs) continue;
+    const int64_t row = h0 + g;  // one query position
+    const float M = s_m[g], L = s_l[g];
+    if constexpr (FINAL) {
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+      reinterpret_cast<__half2*>(a.out + row * D)[pr] = __floats2half2_rn(o0[g] * inv, o1[g] * inv);
+      if (pr == 0 && a.lse != nullptr) a.lse[row] = L > 0.0f ? M + logf(L) : -INFINITY;
+    } else {
+      float* w = a.ws + (row * a.splits + split) * (D + 2);
+      if (pr == 0) {
+        w[0] = nblk > 0 ? M : -INFINITY;
+        w[1] = L;
+      }
+      w[2 + 2 * pr] = o0[g];
+      w[3 + 2 * pr] = o1[g];
+    }
+  }
+}
+
+template <int D, int GB>
+int launch_decode_bulk(AttnArgs& a, cudaStream_t st) {
+  using Cfg = DecCfg<D, GB>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((configured.load() & bit) == 0) {
+    B200_CUDA(cudaFuncSetAttribute(attn_decode_bulk_kernel<D, GB, true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg::smem(Cfg::kRing)));
+    B200_CUDA(cudaFuncSetAttribute(attn_decode_bulk_kernel<D, GB, false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Cfg::smem(Cfg::kRing)));
+    configured.fetch_or(bit);
+  }
+  const int64_t group = a.n_heads / a.n_kv_heads;
+  const dim3 grid(static_cast<unsigned>(a.splits), static_cast<unsigned>(a.n_kv_heads * (group / GB)));
+  unsigned int* err = device_error_word();
+  const unsigned long long lim = wait_limit_ns();
+  // One stage when a split is a single block (more CTAs fit per SM), else two.
+  const int nst = a.chunk <= kDecBlock ? 1 : Cfg::kRing;
+  const size_t smem = static_cast<size_t>(Cfg::smem(nst));
+  if (a.splits == 1) {
+    B200_CUDA(launch_pdl(attn_decode_bulk_kernel<D, GB, true>, grid, dim3(kDecWarps * 32), smem,
+                         st, a, nst, err, lim));
+  } else {
+    B200_CUDA(launch_pdl(attn_decode_bulk_kernel<D, GB, false>, grid, dim3(kDecWarps * 32), smem,
+                         st, a, nst, err, lim));
+    const int64_t total = a.n_heads * D;
+    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(blocks), dim3(256), 0, st, a));
+  }
+  return ENGINE_OK;
+}
+
 __global__ void fill_kernel(float* p, int64_t n, float v) {
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -263,8 +539,18 @@ int run_attention(const __half* q, const __half* k, const __half* v, __half* out
   const int64_t group = n_heads / n_kv_heads;
   const int64_t gb = group % 4 == 0 ? 4 : (group % 2 == 0 ? 2 : 1);
   const int64_t ctas = s_q * n_kv_heads * (group / gb);
+  const bool bulk = s_q == 1 && !causal && stride % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                      reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) % 16) == 0;
   int64_t splits = split_kv;
-  if (splits <= 0) {  // enough CTAs for two per SM, each split at least 128 keys
+  if (splits <= 0 && bulk) {
+    // decode: at least about four CTAs per SM, each split a whole number of
+    // 64-key blocks (one block when the keys allow)
+    const int64_t want = (4 * static_cast<int64_t>(sm_count()) + ctas - 1) / ctas;
+    int64_t chunk = (s_kv + want - 1) / want;
+    chunk = (chunk + kDecBlock - 1) / kDecBlock * kDecBlock;
+    splits = (s_kv + chunk - 1) / chunk;
+  } else if (splits <= 0) {  // enough CTAs for two per SM, each split at least 128 keys
     const int64_t want = (2 * static_cast<int64_t>(sm_count()) + ctas - 1) / ctas;
     const int64_t most = (s_kv + 127) / 128;
     splits = want < most ? want : most;
@@ -285,7 +571,15 @@ int run_attention(const __half* q, const __half* k, const __half* v, __half* out
                    (reinterpret_cast<uintptr_t>(k) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(v) % 16 == 0) && (stride % 8 == 0);
   int rc;
-  if (d == 64) {
+  if (bulk) {
+    if (d == 64) {
+      rc = gb == 4 ? launch_decode_bulk<64, 4>(a, st)
+                   : (gb == 2 ? launch_decode_bulk<64, 2>(a, st) : launch_decode_bulk<64, 1>(a, st));
+    } else {
+      rc = gb == 4 ? launch_decode_bulk<128, 4>(a, st)
+                   : (gb == 2 ? launch_decode_bulk<128, 2>(a, st) : launch_decode_bulk<128, 1>(a, st));
+    }
+  } else if (d == 64) {
     rc = vec ? launch_gb<64, true>(a, st) : launch_gb<64, false>(a, st);
   } else {
     rc = vec ? launch_gb<128, true>(a, st) : launch_gb<128, false>(a, st);
@@ -325,6 +619,17 @@ int engine_cuda_attention_prefill(const engine_half_t* q, const engine_half_t* k
   B200_REQUIRE(std::isfinite(scale), "attention_prefill: scale must be finite");
   B200_REQUIRE(kv_head_stride >= (s_kv > 0 ? s_kv * head_dim : 0),
                "attention_prefill: kv_head_stride < s_kv * head_dim");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  static const int tc_env = env_flag("ENGINE_ATTN_TC", 1);
+  if (tc_env != 0 && s_q >= kAttnTcMinRows && s_kv > 0) {
+    // tcgen05 FlashAttention (attention_tc.cu); shapes or alignments it does not
+    // take fall through to the CUDA-core kernel below.
+    const int rc = attention_prefill_tc(
+        reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
+        reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(out), s_q, s_kv, n_heads,
+        n_kv_heads, head_dim, kv_head_stride, scale, q_pos_offset, is_causal != 0, out_lse, st);
+    if (rc != ENGINE_ERR_UNSUPPORTED) return rc;
+  }
   B200_REQUIRE(s_q <= 65535 && n_heads <= 65535, "attention_prefill: s_q or n_heads too large");
   return run_attention(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
                        reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(out), s_q,

@@ -75,6 +75,13 @@ bool make_tmap_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, 
                   uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                   uint32_t box_cols);
 
+/// 3-D tensor map (dims innermost first, element strides of dims 1 and 2 in
+/// elements), box `box` (innermost first), 128-byte swizzle, zero fill out of
+/// bounds.  Not cached.  Returns false (with the error recorded) on failure.
+bool make_tmap_3d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dtype, int elem_bytes,
+                  const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+                  const uint32_t (&box)[3]);
+
 }  // namespace b200
 
 #define B200_REQUIRE(cond, msg)                                      \

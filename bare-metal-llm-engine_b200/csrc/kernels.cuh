@@ -64,6 +64,14 @@ void scratch_free(void* p, cudaStream_t stream);
 int gemv_nk_norm1_swiglu_f16(const __half* W, const __half* X, const __half* gamma, float eps,
                              __half* Y, int64_t F, int64_t K, cudaStream_t stream);
 
+/// Attention prefill on tcgen05 (attention_tc.cu): the attention_prefill
+/// contract for head_dim 64 / 128.  Returns ENGINE_ERR_UNSUPPORTED, with nothing
+/// launched, when a stride or pointer alignment does not allow its TMA maps.
+int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __half* out,
+                         int64_t s_q, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
+                         int64_t kv_head_stride, float scale, int64_t q_pos_offset, bool causal,
+                         float* lse, cudaStream_t stream);
+
 /// Zeroes the stream-K tile counters of every workspace on `dev` (after a
 /// device-side time-out may have left a launch half counted).  The device must
 /// be idle.  gemm_tc.cu.

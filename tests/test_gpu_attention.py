@@ -146,3 +146,79 @@ def test_decode_throughput_llama8b(pkg, dev):
     us = e0.elapsed_time(e1) / n * 1e3
     byt = 2 * H_kv * kv_len * d * 2 + 2 * 2 * H * d
     print(f"attention_decode Llama-3-8B kv_len=4096: {us:.1f} us, {byt / us / 1e3:.0f} GB/s")
+
+
+# ------------------------------------------------------------------ tcgen05 prefill / bulk decode
+
+@pytest.mark.parametrize("s_q,s_kv,off,causal,h,h_kv,d", [
+    (130, 129, 0, True, 4, 2, 128),     # partial query block and partial key tile
+    (200, 300, 100, True, 8, 8, 64),    # d = 64, MHA, causal with an offset
+    (200, 300, 0, False, 8, 2, 128),    # non-causal, s_q != s_kv
+    (1024, 1024, 0, True, 8, 2, 128),   # eight key tiles, rescales across tiles
+    (16, 700, 684, True, 4, 1, 64),     # the smallest s_q the tensor-core path takes
+])
+def test_prefill_tensor_core_path_matches_oracle(pkg, dev, s_q, s_kv, off, causal, h, h_kv, d):
+    rng = np.random.default_rng(s_q * 7 + s_kv)
+    q, k, v = _rand(rng, s_q, h, h_kv, s_kv, d)
+    want, want_lse = oracle.attention(q, k, v, _scale(d), off, causal)
+    args = [torch.from_numpy(a).to(dev) for a in (q, k, v)]
+    out, lse = pkg.ops.attention(*args, _scale(d), off, causal, want_lse=True)
+    (rt, at), (lrt, lat) = _tol(s_kv)
+    _close(out.cpu().numpy().astype(np.float32), want.astype(np.float32), rt, at, "prefill tc")
+    _close(lse.cpu().numpy(), want_lse, lrt, lat, "prefill tc lse")
+    again, lse2 = pkg.ops.attention(*args, _scale(d), off, causal, want_lse=True)
+    assert torch.equal(out, again) and torch.equal(lse, lse2)  # deterministic
+
+
+def test_prefill_large_scores_and_peaked_rows(pkg, dev):
+    """Scores of magnitude ~50: every row's max moves across tiles and the
+    probabilities underflow for most keys; the online rescaling must agree with
+    the two-pass oracle."""
+    rng = np.random.default_rng(11)
+    q, k, v = _rand(rng, 384, 4, 2, 512, 128, amp=2.5)
+    want, want_lse = oracle.attention(q, k, v, _scale(128), 128, True)
+    out, lse = pkg.ops.attention(*(torch.from_numpy(a).to(dev) for a in (q, k, v)), _scale(128),
+                                 128, True, want_lse=True)
+    (rt, at), (lrt, lat) = _tol(512)
+    _close(out.cpu().numpy().astype(np.float32), want.astype(np.float32), rt, at, "peaked")
+    _close(lse.cpu().numpy(), want_lse, lrt, lat, "peaked lse")
+
+
+@pytest.mark.parametrize("kv_len,h,h_kv,d,split", [
+    (1000, 32, 8, 128, 0), (1000, 8, 8, 64, 0), (777, 16, 8, 128, 5), (64, 4, 2, 64, 0),
+    (1, 4, 4, 128, 0), (8191, 32, 8, 128, 0)])
+def test_decode_bulk_path_matches_oracle(pkg, dev, kv_len, h, h_kv, d, split):
+    rng = np.random.default_rng(kv_len + h)
+    q, k, v = _rand(rng, 1, h, h_kv, kv_len, d)
+    want, _ = oracle.attention(q, k, v, _scale(d), 0, False)
+    qd, kd, vd = (torch.from_numpy(a).to(dev) for a in (q[0], k, v))
+    out = pkg.ops.attention_decode(qd, kd, vd, _scale(d), split)
+    (rt, at), _ = _tol(kv_len)
+    _close(out.cpu().numpy().astype(np.float32), want[0].astype(np.float32), rt, at,
+           f"decode kv_len={kv_len}")
+    assert torch.equal(out, pkg.ops.attention_decode(qd, kd, vd, _scale(d), split))
+
+
+def test_prefill_throughput_llama8b(pkg, dev):
+    """Prints the tcgen05 prefill's rate at Llama-3-8B, S = 2048 causal (not asserted)."""
+    H, H_kv, d, S = 32, 8, 128, 2048
+    q = torch.randn(S, H, d, device=dev).half()
+    k = torch.randn(H_kv, S, d, device=dev).half()
+    v = torch.randn(H_kv, S, d, device=dev).half()
+    out = torch.empty_like(q)
+    st = torch.cuda.current_stream().cuda_stream
+    fn = lambda: pkg.cuda.attention_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(),  # noqa: E731
+                                            out.data_ptr(), S, S, H, H_kv, d, S * d, d ** -0.5,
+                                            0, True, 0, st)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    print(f"attention_prefill Llama-3-8B S=2048 causal: {ms * 1e3:.1f} us, "
+          f"{4.0 * S * S * d * H / 2 / (ms * 1e-3) / 1e12:.0f} TFLOP/s")
