@@ -196,31 +196,67 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const AttnA
   }
 }
 
-// One thread per (row, element): the splits' (m, l, O) combined in split order.
+// One CTA (8 warps) per query row (position x head): the splits' (m, l, O)
+// combined with weights exp(m_s - M), M the largest m_s.  Warp w takes splits
+// w, w + 8, ...: its lanes load O_s as 16-byte (d = 128) or 8-byte (d = 64)
+// vectors, all of a warp's loads independent, so the merge runs at L2 latency,
+// not one round trip per split.  The eight warp sums are added in warp order:
+// deterministic.
+constexpr int kMergeWarps = 8;
 template <int D>
-__global__ void __launch_bounds__(256) attn_merge_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kMergeWarps * 32) attn_merge_kernel(const AttnArgs a) {
+  constexpr int EPL = D / 32;  // elements per lane
+  __shared__ float s_o[kMergeWarps][D];
+  __shared__ float s_l[kMergeWarps];
+  __shared__ float s_m[kMergeWarps];
   pdl_trigger();
   pdl_wait();
-  const int64_t rows = a.s_q * a.n_heads;
-  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < rows * D;
-       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = t / D;
-    const int d = static_cast<int>(t % D);
-    const float* w = a.ws + row * a.splits * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, w[s * (D + 2)]);
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < a.splits; ++s) {
-        const float ms = w[s * (D + 2)];
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - M);
-        L = fmaf(w[s * (D + 2) + 1], f, L);
-        O = fmaf(w[s * (D + 2) + 2 + d], f, O);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int S = a.splits;
+  for (int64_t row = blockIdx.x; row < a.s_q * a.n_heads; row += gridDim.x) {
+    const float* w = a.ws + row * static_cast<int64_t>(S) * (D + 2);
+    float mx = -INFINITY;
+    for (int sp = t; sp < S; sp += kMergeWarps * 32) mx = fmaxf(mx, w[static_cast<int64_t>(sp) * (D + 2)]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_m[warp] = mx;
+    __syncthreads();
+    float M = s_m[0];
+#pragma unroll
+    for (int i = 1; i < kMergeWarps; ++i) M = fmaxf(M, s_m[i]);
+    float o[EPL], L = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
+#pragma unroll 4
+    for (int sp = warp; sp < S; sp += kMergeWarps) {
+      const float* ws = w + static_cast<int64_t>(sp) * (D + 2);
+      const float ms = ws[0];
+      const float f = (ms == -INFINITY || M == -INFINITY) ? 0.0f : expf(ms - M);
+      L = fmaf(ws[1], f, L);
+      // O_s starts at an 8-byte boundary (D + 2 floats per split): two float2 per lane for
+      // d = 128, one for d = 64
+#pragma unroll
+      for (int e = 0; e < EPL; e += 2) {
+        const float2 v = *reinterpret_cast<const float2*>(ws + 2 + lane * EPL + e);
+        o[e] = fmaf(v.x, f, o[e]);
+        o[e + 1] = fmaf(v.y, f, o[e + 1]);
       }
     }
-    a.out[row * D + d] = __float2half_rn(L > 0.0f ? O / L : 0.0f);
-    if (d == 0 && a.lse != nullptr) a.lse[row] = L > 0.0f ? M + logf(L) : -INFINITY;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s_o[warp][lane * EPL + e] = o[e];
+    if (lane == 0) s_l[warp] = L;
+    __syncthreads();
+    if (t < D) {
+      float Ot = 0.0f, Lt = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kMergeWarps; ++i) {
+        Ot += s_o[i][t];
+        Lt += s_l[i];
+      }
+      a.out[row * D + t] = __float2half_rn(Lt > 0.0f ? Ot / Lt : 0.0f);
+      if (t == 0 && a.lse != nullptr) a.lse[row] = Lt > 0.0f ? M + logf(Lt) : -INFINITY;
+    }
+    __syncthreads();  // s_o / s_m are reused by the next row
   }
 }
 
@@ -258,7 +294,7 @@ __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, ui
 }
 
 template <int D, int GB, bool FINAL>
-__global__ void __launch_bounds__(kDecWarps * 32)
+__global__ void __launch_bounds__(kDecWarps * 32, 4)
     attn_decode_bulk_kernel(const AttnArgs a, int nst, unsigned int* err,
                             unsigned long long limit_ns) {
   using Cfg = DecCfg<D, GB>;
@@ -482,9 +518,8 @@ int launch_decode_bulk(AttnArgs& a, cudaStream_t st) {
   } else {
     B200_CUDA(launch_pdl(attn_decode_bulk_kernel<D, GB, false>, grid, dim3(kDecWarps * 32), smem,
                          st, a, nst, err, lim));
-    const int64_t total = a.n_heads * D;
-    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
-    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(blocks), dim3(256), 0, st, a));
+    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(static_cast<unsigned>(a.n_heads)),
+                         dim3(kMergeWarps * 32), 0, st, a));
   }
   return ENGINE_OK;
 }
@@ -504,10 +539,9 @@ int launch_split(AttnArgs& a, cudaStream_t st) {
     B200_CUDA(launch_pdl(attn_split_kernel<D, GB, VEC, true>, grid, dim3(kAttnWarps * 32), 0, st, a));
   } else {
     B200_CUDA(launch_pdl(attn_split_kernel<D, GB, VEC, false>, grid, dim3(kAttnWarps * 32), 0, st, a));
-    const int64_t total = a.s_q * a.n_heads * D;
-    const int64_t blocks64 = (total + 255) / 256;
-    const unsigned blocks = static_cast<unsigned>(blocks64 < 65535 ? blocks64 : 65535);
-    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(blocks), dim3(256), 0, st, a));
+    const int64_t rows = a.s_q * a.n_heads;
+    B200_CUDA(launch_pdl(attn_merge_kernel<D>, dim3(static_cast<unsigned>(rows < 65535 ? rows : 65535)),
+                         dim3(kMergeWarps * 32), 0, st, a));
   }
   return ENGINE_OK;
 }

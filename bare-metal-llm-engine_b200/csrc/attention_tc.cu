@@ -59,7 +59,7 @@ constexpr int kAtBN = 128;       // keys per tile
 constexpr int at_threads(int ns) { return 64 + 128 * ns; }
 constexpr float kAtRescale = 8.0f;
 #ifndef ENGINE_ATTN_NS128
-#define ENGINE_ATTN_NS128 4
+#define ENGINE_ATTN_NS128 2
 #endif
 #ifndef ENGINE_ATTN_NS64
 #define ENGINE_ATTN_NS64 2
@@ -94,6 +94,15 @@ struct AtParams {
   unsigned int* err;
   unsigned long long limit_ns;
 };
+
+/// 2^x by the MUFU approximation (ex2.approx.ftz.f32, relative error ~2^-22;
+/// results below 2^-126 flush to zero -- probabilities that small vanish in the
+/// FP16 P tile anyway).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 /// Keys visible to query row `row` (global index), as the last visible index.
 __device__ __forceinline__ int64_t at_last_key(const AtParams& p, int64_t row) {
@@ -299,7 +308,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;
-      bool w = mbar_wait(&s_full[b], (j >> 1) & 1u, p.limit_ns, p.err);
+      bool w = mbar_wait_sleepy(&s_full[b], (j >> 1) & 1u, p.limit_ns, p.err);
       if (!__all_sync(0xffffffffu, w)) {
         ok = false;
         break;
@@ -326,7 +335,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       if constexpr (NS > 1) {
         s_mx[b][cg][r] = mt;
         mbar_arrive(&xbar[b][q4]);
-        w = mbar_wait(&xbar[b][q4], (j >> 1) & 1u, p.limit_ns, p.err);
+        w = mbar_wait_sleepy(&xbar[b][q4], (j >> 1) & 1u, p.limit_ns, p.err);
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
@@ -344,15 +353,15 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       const float m_new = (first || rescale) ? fmaxf(m, mt) : m;
       // With no visible key yet the row keeps m = -inf and P = 0.
       const float base = (m_new == -INFINITY) ? 0.0f : m_new;
-      const float alpha = exp2f(m - base);  // m = -inf -> 0; no rescale -> 1
+      const float alpha = ex2_fast(m - base);  // m = -inf -> 0; no rescale -> 1
       float ls = 0.0f;
       uint32_t pk[CW / 32][16];
 #pragma unroll
       for (int c = 0; c < CW / 32; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = exp2f(__uint_as_float(sv[c][e]) - base);
-          const float p1 = exp2f(__uint_as_float(sv[c][e + 1]) - base);
+          const float p0 = ex2_fast(__uint_as_float(sv[c][e]) - base);
+          const float p1 = ex2_fast(__uint_as_float(sv[c][e + 1]) - base);
           ls += p0 + p1;
           __half2 hv = __floats2half2_rn(p0, p1);
           pk[c][e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
@@ -362,18 +371,19 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       m = m_new;
       // The P tile and O hold tile j-1's product once that PV completed.
       if (j >= 1) {
-        w = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1u, p.limit_ns, p.err);
+        w = mbar_wait_sleepy(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1u, p.limit_ns, p.err);
         if (!__all_sync(0xffffffffu, w)) {
           ok = false;
           break;
         }
       }
-      uint8_t* prow = sP + (cg * CW / 64) * 16384 + r * 128;  // sub-tile of keys 0-63 / 64-127
 #pragma unroll
       for (int c = 0; c < CW / 32; ++c) {
+        const int key = cg * CW + c * 32;  // first key of these 32
+        uint8_t* prow = sP + (key >> 6) * 16384 + r * 128;  // sub-tile of keys 0-63 / 64-127
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int chunk = (((cg * CW) & 63) >> 3) + c * 4 + q;  // 16-byte chunk of the row
+          const int chunk = ((key & 63) >> 3) + q;  // 16-byte chunk of the 128-byte row
           *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(pk[c][4 * q], pk[c][4 * q + 1], pk[c][4 * q + 2], pk[c][4 * q + 3]);
         }
@@ -399,14 +409,14 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     if (NS > 1 && ok) {
       s_lx[cg][r] = l;
       mbar_arrive(&lbar[q4]);
-      ok = __all_sync(0xffffffffu, mbar_wait(&lbar[q4], 0, p.limit_ns, p.err));
+      ok = __all_sync(0xffffffffu, mbar_wait_sleepy(&lbar[q4], 0, p.limit_ns, p.err));
       l = 0.0f;
 #pragma unroll
       for (int g = 0; g < NS; ++g) l += s_lx[g][r];
     }
     if (ok) {
       const int last = ntiles - 1;
-      const bool w = mbar_wait(&o_done[last & 1], (last >> 1) & 1u, p.limit_ns, p.err);
+      const bool w = mbar_wait_sleepy(&o_done[last & 1], (last >> 1) & 1u, p.limit_ns, p.err);
       if (__all_sync(0xffffffffu, w)) {
         tc_fence_after();
         const float inv = 1.0f / l;

@@ -101,6 +101,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+/// try_wait with an explicit suspend-time hint (ns): a waiting thread may stay
+/// suspended up to that long instead of the system default, so waiters that
+/// are not on a critical path take fewer issue slots from the warps that are.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+/// mbar_wait for consumer threads that can sleep: the same bound, with the
+/// suspend hint on every poll.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity,
+                                                 unsigned long long limit_ns, unsigned int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long deadline = globaltimer() + limit_ns;
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+    if (globaltimer() > deadline) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
 /// Waits for the phase of parity `parity` of `bar` to complete.  Returns false
 /// (after setting kErrWaitTimeout in `err`) if it has not completed within
 /// `limit_ns` nanoseconds of the first failed poll.  Never spins without limit.

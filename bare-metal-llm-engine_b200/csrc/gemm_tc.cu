@@ -162,14 +162,9 @@ __device__ __forceinline__ void store16(void* p, int64_t i, float v) {
 #ifndef ENGINE_TC_GROUP
 #define ENGINE_TC_GROUP 8
 #endif
-// 2-SM kernel: shared-memory stages (0 = the default for the tile width) and the
-// distance, in k-blocks, of its L2 prefetch of operand tiles ahead of the TMA
-// loads (0 = off).
+// 2-SM kernel: shared-memory stages (0 = the default for the tile width).
 #ifndef ENGINE_TC2_STAGES
 #define ENGINE_TC2_STAGES 0
-#endif
-#ifndef ENGINE_TC2_L2PF
-#define ENGINE_TC2_L2PF 0
 #endif
 
 __device__ __forceinline__ void tile_coords(int64_t t, int tiles_m, int tiles_n, int& tm,
@@ -833,24 +828,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + s * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kABytes;
-          if constexpr (ENGINE_TC2_L2PF > 0) {
-            // Warm L2 with this CTA's operand tiles ENGINE_TC2_L2PF k-blocks ahead,
-            // so that the first reader of a panel slice waits on L2, not DRAM.
-            const int64_t kp = kb + ENGINE_TC2_L2PF;
-            if (kp < w.kb1) {
-              tma_prefetch_2d(&tmA, static_cast<int32_t>(kp * kBK),
-                              tm * 256 + static_cast<int>(rank) * 128);
-              if constexpr (B_MN) {
-#pragma unroll
-                for (int j = 0; j < BN / 128; ++j)
-                  tma_prefetch_2d(&tmB, tn * BN + static_cast<int>(rank) * (BN / 2) + j * 64,
-                                  static_cast<int32_t>(kp * kBK));
-              } else {
-                tma_prefetch_2d(&tmB, static_cast<int32_t>(kp * kBK),
-                                tn * BN + static_cast<int>(rank) * (BN / 2));
-              }
-            }
-          }
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
           const uint32_t fbar = full_leader0 + s * 8;
           tma_load_2d_2sm(sa, &tmA, fbar, static_cast<int32_t>(kb * kBK),
@@ -1275,6 +1252,7 @@ int gemm_tc_general(const void* A, const void* B, const void* residual, void* C,
   if (rc != ENGINE_OK) return rc;
   return check_launch("matmul/linear (tcgen05)");
 }
+
 
 /// With hilo=true, A holds 2*half_b activation rows (FP16 roundings, then the
 /// FP16 roundings of the remainders) of a batch padded to half_b rows, b_kmajor

@@ -310,6 +310,37 @@ def test_rmsnorm_linear_f16_residual(pkg, dev, M):
     bounds.check(host(Y).astype(np.float32), exact, bound, f"resid M={M}")
 
 
+@pytest.mark.parametrize("M,N,K,gamma,resid", [
+    (7, 300, 1000, True, False),     # partial weight tile, last k-block partial (K % 64 = 40)
+    (32, 640, 4104, True, True),     # 32 rows (64 hi/lo activation rows), residual
+    (5, 128, 64, False, False),      # one k-block, no gamma
+    (16, 6144, 14336, True, False),  # long K: split-K cluster partials and row sums
+])
+def test_rmsnorm_linear_f16_hilo_edges(pkg, dev, M, N, K, gamma, resid):
+    """5 <= M <= 32 (hi/lo activations, swap-AB tcgen05, split-K clusters) at the
+    edges of its tiling: a partial weight tile, a partial last k-block, a single
+    k-block, 32 rows, a long K; run twice for determinism."""
+    rng = np.random.default_rng(M + N + K)
+    x = f16(rng, (M, K))
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float16) if gamma else None
+    W = f16(rng, (N, K), 0.02)
+    R = f16(rng, (M, N)) if resid else None
+    Y = torch.empty(M, N, device=dev, dtype=torch.float16)
+    pkg.cuda.rmsnorm_linear_f16(dev_t(x).data_ptr(), dev_t(g).data_ptr() if gamma else 0,
+                                dev_t(W).data_ptr(), dev_t(R).data_ptr() if resid else 0,
+                                Y.data_ptr(), M, N, K, EPS)
+    _, exact = oracle.rmsnorm_linear_f16(x, g, W, EPS, residual=R, want_f32=True, nthreads=8)
+    t = oracle.rmsnorm(x.astype(np.float32), None if g is None else g.astype(np.float32), EPS)
+    absdot = np.abs(t.astype(np.float64)) @ np.abs(W.astype(np.float64)).T
+    bound = rms_bound(M, K, absdot, exact) + (bounds.U16 * np.abs(exact) if resid else 0)
+    bounds.check(host(Y).astype(np.float32), exact, bound, f"hilo M={M} N={N} K={K}")
+    Y2 = torch.empty_like(Y)
+    pkg.cuda.rmsnorm_linear_f16(dev_t(x).data_ptr(), dev_t(g).data_ptr() if gamma else 0,
+                                dev_t(W).data_ptr(), dev_t(R).data_ptr() if resid else 0,
+                                Y2.data_ptr(), M, N, K, EPS)
+    assert torch.equal(Y, Y2)  # fixed-order cluster reduction: deterministic
+
+
 @pytest.mark.parametrize("M,F,gamma", [(1, 1792, True), (1, 14336, True), (1, 3584, False),
                                        (3, 1792, True), (16, 3584, True)])
 def test_rmsnorm_linear_swiglu_fused(pkg, dev, M, F, gamma):
