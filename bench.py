@@ -861,8 +861,10 @@ def run_headline(args):
 
 
 KERNEL_CASES = ("gemm4096", "gemv_4096x14336", "rmsnorm_qkv_b1", "rmsnorm_qkv_b16",
-                "matmul_f32_512", "prefill_s2048", "gate_up_swiglu_b1", "tp_down_b1_world1",
-                "gemv_q8_0_4096x14336", "gemv_q4_0_4096x14336")
+                "matmul_f32_512", "matmul_f32_4096", "prefill_s2048", "gate_up_swiglu_b1",
+                "tp_down_b1_world1", "tp_allreduce_b32_world1", "gemv_q8_0_4096x14336",
+                "gemv_q4_0_4096x14336", "gemv_fp16_kn_4096", "attn_prefill_s2048",
+                "attn_decode_4096")
 
 
 def run_kernel_case(args) -> int:
@@ -920,6 +922,42 @@ def run_kernel_case(args) -> int:
                  torch.empty(1, N, device=dev, dtype=torch.float16)) for _ in range(4)]
         fn = lambda s: pkg.cuda.tp_linear_allreduce_f16(comm.handle, s[0].data_ptr(), s[1].data_ptr(),  # noqa: E731
                                                         s[2].data_ptr(), s[3].data_ptr(), 1, N, K, st)
+    elif c == "matmul_f32_4096":  # the reference's FP32 headline size
+        n = 4096
+        sets = [(torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.rand(n, n, device=dev, generator=g) * 2 - 1,
+                 torch.empty(n, n, device=dev)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.matmul_register_tiled(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), n, n, n, st)  # noqa: E731
+    elif c == "tp_allreduce_b32_world1":  # the communicator's all-reduce, 32 x 4096, one rank
+        comm = pkg.tp.NvlinkComm(0, 1, 32 * 4096)
+        sets = [(torch.randn(32 * 4096, device=dev, generator=g).half(),
+                 torch.empty(32 * 4096, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.tp_allreduce_f16(comm.handle, s[0].data_ptr(), 0, s[1].data_ptr(),  # noqa: E731
+                                                 32 * 4096, st)
+    elif c == "gemv_fp16_kn_4096":  # the legacy gemv_fp16, A[K, N] 4096 x 4096
+        N = K = 4096
+        sets = [((torch.randn(K, N, device=dev, generator=g) * 0.02).half(),
+                 torch.randn(K, device=dev, generator=g).half(),
+                 torch.empty(N, device=dev, dtype=torch.float16)) for _ in range(6)]
+        fn = lambda s: pkg.cuda.gemv_fp16(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), N, K, st)  # noqa: E731
+    elif c == "attn_prefill_s2048":  # Llama-3-8B heads, causal, S = 2048 (tcgen05)
+        S, H, Hk, d = 2048, 32, 8, 128
+        sets = [(torch.randn(S, H, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, S, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, S, d, device=dev, generator=g).half(),
+                 torch.empty(S, H, d, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.attention_prefill(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                                                  s[3].data_ptr(), S, S, H, Hk, d, S * d, d ** -0.5,
+                                                  0, True, 0, st)
+    elif c == "attn_decode_4096":  # one token over 4096 keys, Llama-3-8B heads
+        kv, H, Hk, d = 4096, 32, 8, 128
+        sets = [(torch.randn(H, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.empty(H, d, device=dev, dtype=torch.float16)) for _ in range(8)]
+        fn = lambda s: pkg.cuda.attention_decode(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                                                 s[3].data_ptr(), kv, H, Hk, d, kv * d, d ** -0.5, 0,
+                                                 st)
     elif c.startswith("gemv_q"):  # block-quantised decode GEMV, streamed layout (timing only)
         N, K = 4096, 14336
         qt = 8 if c.startswith("gemv_q8") else 4
