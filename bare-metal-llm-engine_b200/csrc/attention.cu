@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) attn_merge_kernel(const Attn
 // are contiguous ([n_kv_heads][kv_head_stride], key j at j * d), so a CTA's
 // split arrives as whole 64-key blocks of K and of V, each ONE cp.async.bulk
 // into a two-stage shared-memory ring: all of a block's bytes are in flight at
-// once.  Per block the CTA (4 warps, GB query heads of one KV group) forms the
+// once.  Per block the CTA (8 warps, GB query heads of one KV group) forms the
 // scores (lane groups of d/8 lanes per key, shuffle-reduced), the block max and
 // probabilities per head, and O = alpha * O + P V with one thread per output
 // pair of elements -- one rescale per 64 keys, not per key.  The split's
