@@ -17,26 +17,31 @@
 //               over [s_q][n_heads][d]), then K and V tiles of 128 keys into
 //               two-stage rings (3-D maps over [n_kv_heads][keys][d]; zero fill
 //               past s_kv);
-//   warp 1      allocates TMEM (two 128-column S accumulators and a D-column O
-//               accumulator) and one thread issues tcgen05.mma: S[j] = Q K[j]^T
-//               (A = Q, B = K, both K-major, M = N = 128), then O += P[j-1] V[j-1]
-//               (A = P from shared memory, B = V MN-major, N = d), so the
-//               scores of tile j are formed while the softmax of tile j-1 runs;
+//   warp 1      allocates TMEM (three 128-column S / P buffers and a D-column
+//               O accumulator) and one thread issues tcgen05.mma: S[j] = Q K[j]^T
+//               into buffer j % 3 (A = Q, B = K, both K-major, M = N = 128), then
+//               O += P[j-1] V[j-1] with A = P[j-1] read from tensor memory and
+//               B = V (MN-major, N = d), so the scores of tile j are formed while
+//               the softmax of tile j-1 runs; S[j] waits only for the PV product
+//               that last read its buffer (tile j-3);
 //   warps 2..   the softmax, NS threads per query row: warp w reads TMEM lanes
 //               32*(w%4)..+31 (its rows) and column group (w-2)/4 of them, so
 //               NS warps share each lane quarter (the MUFU and FMA work of a
 //               tile spreads over 4*NS warps).  A thread reads its slice of S
 //               with tcgen05.ld, masks keys past s_kv and above the causal
-//               diagonal; the row max is combined across the row's threads
-//               through shared memory (bounded mbarrier exchange); it keeps the
-//               running max m (base-2 domain) and its partial sum l in FP32,
-//               writes P = exp2(S*c - m) as FP16 into the 128-byte-swizzled P
-//               tile (the A operand of the PV product) once the previous PV
-//               product completed, and when the row max grew by more than 2^8
-//               rescales its slice of O in TMEM (tcgen05.ld / st); below that,
-//               P <= 2^8 is kept against the old max.  At the end the partial
-//               sums are added in column-group order, O is read, divided by l,
-//               rounded once to FP16 and stored, and lse = m ln 2 + ln l.
+//               diagonal; the row max (of the raw scores: the scale c > 0 is
+//               folded into one FMA before ex2) is combined across the row's
+//               threads through shared memory (bounded mbarrier exchange); it
+//               keeps the running max m (base-2 domain) and its partial sum l
+//               in FP32 and writes P = exp2(S*c - m) as FP16 pairs with
+//               tcgen05.st over the first 64 columns of the same buffer -- no
+//               shared-memory round trip and no wait for the previous PV
+//               product.  When the row max grew by more than 2^8 it rescales
+//               its slice of O in TMEM (tcgen05.ld / st, after PV[j-1]); below
+//               that, P <= 2^8 is kept against the old max.  At the end the
+//               partial sums are added in column-group order, O is read,
+//               divided by l, rounded once to FP16 and stored, and
+//               lse = m ln 2 + ln l.
 // Tiles of keys entirely above the causal diagonal are never loaded.  The sum l
 // is formed from the FP32 probabilities; P enters the tensor cores rounded to
 // FP16 (relative error <= 2^-11 per probability).
@@ -73,14 +78,13 @@ struct AtCfg {
   static constexpr int kQBytes = kAtBM * D * 2;
   static constexpr int kKBytes = kAtBN * D * 2;
   static constexpr int kVBytes = kAtBN * D * 2;
-  static constexpr int kPBytes = kAtBM * kAtBN * 2;
   static constexpr int kStages = 2;
   static constexpr int kOffK = kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKBytes;
-  static constexpr int kOffP = kOffV + kStages * kVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
+  static constexpr int kOffBar = kOffV + kStages * kVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-  static constexpr int kTmemCols = 512;  // S0, S1 (128 each), O (D)
+  static constexpr int kTmemCols = 512;  // S / P buffers 0-2 (128 columns each), O (D)
+  static constexpr int kOCol = 3 * kAtBN;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -123,17 +127,16 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
   uint8_t* sQ = smem;
   uint8_t* sK = smem + Cfg::kOffK;
   uint8_t* sV = smem + Cfg::kOffV;
-  uint8_t* sP = smem + Cfg::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* q_full = bars;          // 1
   uint64_t* k_full = bars + 1;      // ST
   uint64_t* k_empty = k_full + ST;  // ST
   uint64_t* v_full = k_empty + ST;  // ST
   uint64_t* v_empty = v_full + ST;  // ST
-  uint64_t* s_full = v_empty + ST;  // 2
-  uint64_t* p_full = s_full + 2;    // 2
-  uint64_t* o_done = p_full + 2;    // 2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  uint64_t* s_full = v_empty + ST;  // 3: S(j) in buffer j % 3 complete
+  uint64_t* p_full = s_full + 3;    // 3: P(j) written over it
+  uint64_t* o_done = p_full + 3;    // 3: PV(j) complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 3);
   static_assert(kAtBN % (32 * NS) == 0 && D % (32 * NS) == 0, "column groups of 32");
   __shared__ float s_mx[2][NS][kAtBM];  // per-row exchange of the column groups' maxima
   __shared__ float s_lx[NS][kAtBM];     // ... and of their sums, at the end
@@ -159,7 +162,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 3; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128 * NS);
       mbar_init(&o_done[b], 1);
@@ -229,43 +232,43 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     if (lane == 0) {
       constexpr uint32_t kIdescS = umma_idesc_f16(128, kAtBN, false, false, false);
       constexpr uint32_t kIdescO = umma_idesc_f16(128, D, false, false, true);
-      const uint32_t tO = tmem_base + 256;
+      const uint32_t tO = tmem_base + Cfg::kOCol;
       bool ok = mbar_wait(q_full, 0, p.limit_ns, p.err);
       const uint32_t q_addr = smem_u32(sQ);
-      auto pv = [&](int i) {  // O += P[i] V[i]
-        const int b = i & 1;
+      auto pv = [&](int i) {  // O += P[i] V[i], P[i] in TMEM over S[i]
+        const int b = i % 3;
         const int s = i % ST;
-        if (!mbar_wait(&p_full[b], (i >> 1) & 1u, p.limit_ns, p.err)) return false;
+        if (!mbar_wait(&p_full[b], (i / 3) & 1u, p.limit_ns, p.err)) return false;
         if (!mbar_wait(&v_full[s], (i / ST) & 1u, p.limit_ns, p.err)) return false;
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP);
+        const uint32_t pa = tmem_base + b * kAtBN;
         const uint32_t va = smem_u32(sV + s * Cfg::kVBytes);
 #pragma unroll
         for (int kk = 0; kk < kAtBN / 16; ++kk) {
-          const uint64_t adesc = umma_desc_sw128(pa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
           const uint64_t bdesc =
               umma_desc_sw128(va + (kk >> 2) * (Cfg::kDH * 8192) + (kk & 3) * 2048, 8192, 1024);
-          umma_f16(tO, adesc, bdesc, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tO, pa + kk * 8, bdesc, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&v_empty[s]);
         umma_commit(&o_done[b]);
         return true;
       };
       int last_s = -1, last_pv = -1;  // last S / PV products issued
-      auto pv_tracked = [&](int i) {
-        const bool r = pv(i);
-        if (r) last_pv = i;
-        return r;
-      };
       for (int j = 0; ok && j < ntiles; ++j) {
         const int s = j % ST;
+        const int b = j % 3;
         if (!mbar_wait(&k_full[s], (j / ST) & 1u, p.limit_ns, p.err)) {
+          ok = false;
+          break;
+        }
+        // Buffer b last held P(j-3): its PV product must have read it.
+        if (j >= 3 && !mbar_wait(&o_done[b], ((j - 3) / 3) & 1u, p.limit_ns, p.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t ka = smem_u32(sK + s * Cfg::kKBytes);
-        const uint32_t tS = tmem_base + (j & 1) * 128;
+        const uint32_t tS = tmem_base + b * kAtBN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t adesc = umma_desc_sw128(q_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
@@ -273,18 +276,21 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
           umma_f16(tS, adesc, bdesc, kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&k_empty[s]);
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[b]);
         last_s = j;
-        if (j >= 1 && !pv_tracked(j - 1)) ok = false;
+        if (j >= 1) {
+          if (pv(j - 1)) last_pv = j - 1;
+          else ok = false;
+        }
       }
-      if (ok) pv_tracked(ntiles - 1);
+      if (ok && pv(ntiles - 1)) last_pv = ntiles - 1;
       // No MMA may still use TMEM or shared memory when the CTA leaves: each
       // commit arrives once every earlier MMA completed, so wait (bounded) for
       // the later of the last two commits.
       if (last_pv >= 0 && last_pv >= last_s) {
-        mbar_wait(&o_done[last_pv & 1], (last_pv >> 1) & 1u, p.limit_ns, p.err);
+        mbar_wait(&o_done[last_pv % 3], (last_pv / 3) & 1u, p.limit_ns, p.err);
       } else if (last_s >= 0) {
-        mbar_wait(&s_full[last_s & 1], (last_s >> 1) & 1u, p.limit_ns, p.err);
+        mbar_wait(&s_full[last_s % 3], (last_s / 3) & 1u, p.limit_ns, p.err);
       }
     }
     __syncwarp();
@@ -303,35 +309,46 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     const int64_t row = q0 + r;
     const int64_t lim = at_last_key(p, row);
     const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
-    const uint32_t tO = tmem_base + lane_base + 256 + cg * OW;
+    const uint32_t tO = tmem_base + lane_base + Cfg::kOCol + cg * OW;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
-      bool w = mbar_wait_sleepy(&s_full[b], (j >> 1) & 1u, p.limit_ns, p.err);
+      const int b = j & 1;   // parity of the max exchange
+      const int b3 = j % 3;  // S / P buffer
+      bool w = mbar_wait_sleepy(&s_full[b3], (j / 3) & 1u, p.limit_ns, p.err);
       if (!__all_sync(0xffffffffu, w)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t sv[CW / 32][32];
-      const uint32_t tS = tmem_base + lane_base + b * 128 + cg * CW;
+      const uint32_t tS = tmem_base + lane_base + b3 * kAtBN + cg * CW;
 #pragma unroll
       for (int c = 0; c < CW / 32; ++c) tmem_ld_32x32b_x32(tS + c * 32, sv[c]);
       tmem_wait_ld();
       const int64_t k0 = static_cast<int64_t>(j) * kAtBN + cg * CW;  // first key of this thread
       const bool full = k0 + CW - 1 <= lim;  // none of this thread's keys is masked
-      float mt = -INFINITY;
+      // Raw scores: the scale c > 0 is folded into the exponent below, so the
+      // row max is taken on S itself (c * max S = max c S).
+      float mt0 = -INFINITY, mt1 = -INFINITY;
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < CW / 32; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (k0 + c * 32 + e > lim) sv[c][e] = __float_as_uint(-INFINITY);
+          }
+        }
+      }
 #pragma unroll
       for (int c = 0; c < CW / 32; ++c) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(sv[c][e]) * p.c;
-          if (!full && k0 + c * 32 + e > lim) x = -INFINITY;
-          sv[c][e] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
+        for (int e = 0; e < 32; e += 2) {
+          mt0 = fmaxf(mt0, __uint_as_float(sv[c][e]));
+          mt1 = fmaxf(mt1, __uint_as_float(sv[c][e + 1]));
         }
       }
+      float mt = fmaxf(mt0, mt1);
       if constexpr (NS > 1) {
         s_mx[b][cg][r] = mt;
         mbar_arrive(&xbar[b][q4]);
@@ -343,6 +360,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
 #pragma unroll
         for (int g = 0; g < NS; ++g) mt = fmaxf(mt, s_mx[b][g][r]);
       }
+      mt *= p.c;  // base-2 domain
       // Lazy rescaling: the row keeps its reference max m until a tile's max
       // exceeds it by more than kAtRescale (base 2), so P = exp2(S*c - m) stays
       // below 2^kAtRescale (exact enough in FP16) and O needs rescaling only on
@@ -354,41 +372,39 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       // With no visible key yet the row keeps m = -inf and P = 0.
       const float base = (m_new == -INFINITY) ? 0.0f : m_new;
       const float alpha = ex2_fast(m - base);  // m = -inf -> 0; no rescale -> 1
-      float ls = 0.0f;
-      uint32_t pk[CW / 32][16];
+      float ls0 = 0.0f, ls1 = 0.0f;
+      uint32_t pk[CW / 32][16];  // P as FP16 pairs
 #pragma unroll
       for (int c = 0; c < CW / 32; ++c) {
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2_fast(__uint_as_float(sv[c][e]) - base);
-          const float p1 = ex2_fast(__uint_as_float(sv[c][e + 1]) - base);
-          ls += p0 + p1;
+          const float p0 = ex2_fast(fmaf(__uint_as_float(sv[c][e]), p.c, -base));
+          const float p1 = ex2_fast(fmaf(__uint_as_float(sv[c][e + 1]), p.c, -base));
+          ls0 += p0;
+          ls1 += p1;
           __half2 hv = __floats2half2_rn(p0, p1);
           pk[c][e >> 1] = *reinterpret_cast<uint32_t*>(&hv);
         }
       }
-      l = l * alpha + ls;
+      l = l * alpha + (ls0 + ls1);
       m = m_new;
-      // The P tile and O hold tile j-1's product once that PV completed.
-      if (j >= 1) {
-        w = mbar_wait_sleepy(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1u, p.limit_ns, p.err);
-        if (!__all_sync(0xffffffffu, w)) {
-          ok = false;
-          break;
-        }
-      }
+      // P(j) goes over this thread's row of S(j) in TMEM: keys [cg*CW, +CW) as
+      // CW/2 packed columns from column cg*CW/2.  The row's other threads have
+      // already read their S (they arrived at the max exchange after
+      // tcgen05.wait::ld), so no score is overwritten before it is read.
+      const uint32_t tP = tmem_base + lane_base + b3 * kAtBN + cg * (CW / 2);
 #pragma unroll
-      for (int c = 0; c < CW / 32; ++c) {
-        const int key = cg * CW + c * 32;  // first key of these 32
-        uint8_t* prow = sP + (key >> 6) * 16384 + r * 128;  // sub-tile of keys 0-63 / 64-127
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((key & 63) >> 3) + q;  // 16-byte chunk of the 128-byte row
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[c][4 * q], pk[c][4 * q + 1], pk[c][4 * q + 2], pk[c][4 * q + 3]);
+      for (int c = 0; c < CW / 32; ++c) tmem_st_32x32b_x16(tP + c * 16, pk[c]);
+      // O may be rescaled only once PV(j-1) completed (PV(j) waits for p_full).
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
+      if (any_rescale) {
+        if (j >= 1) {
+          w = mbar_wait_sleepy(&o_done[(j - 1) % 3], ((j - 1) / 3) & 1u, p.limit_ns, p.err);
+          if (!__all_sync(0xffffffffu, w)) {
+            ok = false;
+            break;
+          }
         }
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < OW / 32; ++c) {
@@ -399,11 +415,10 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
           for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
           tmem_st_32x32b_x32(tO + c * 32, ov);
         }
-        tmem_wait_st();
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[b]);
+      mbar_arrive(&p_full[b3]);
     }
     // Row sums: the NS partial sums of a row, added in column-group order.
     if (NS > 1 && ok) {
@@ -416,7 +431,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     }
     if (ok) {
       const int last = ntiles - 1;
-      const bool w = mbar_wait_sleepy(&o_done[last & 1], (last >> 1) & 1u, p.limit_ns, p.err);
+      const bool w = mbar_wait_sleepy(&o_done[last % 3], (last / 3) & 1u, p.limit_ns, p.err);
       if (__all_sync(0xffffffffu, w)) {
         tc_fence_after();
         const float inv = 1.0f / l;
@@ -482,7 +497,8 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
                          int64_t s_q, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
                          int64_t kv_head_stride, float scale, int64_t q_pos_offset, bool causal,
                          float* lse, cudaStream_t stream) {
-  if ((d != 64 && d != 128) || kv_head_stride % 8 != 0 || s_q > (int64_t{1} << 31) ||
+  if ((d != 64 && d != 128) || !(scale > 0.0f) || kv_head_stride % 8 != 0 ||
+      s_q > (int64_t{1} << 31) ||
       (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) % 16 != 0 ||
       s_kv > (int64_t{1} << 31) || n_heads > 65535 || n_kv_heads > 65535)
