@@ -12,18 +12,21 @@
 //
 // One CTA owns 128 query rows of one head (grid: q-blocks x heads, the
 // q-blocks with the most keys first) and runs 64 + 128 * NS threads in three
-// roles:
+// roles.  By default two CTAs share an SM (NB = 1 below: 96 KB of shared
+// memory and 256 TMEM columns each); each CTA's chain S -> softmax -> PV is
+// serial, and the two chains interleave on the tensor cores.  NB = 3 (one CTA
+// per SM, three S / P buffers, two-stage K / V rings) overlaps them inside one
+// CTA instead; on B200 it was 17% slower at S = 2048.
 //   warp 0      one elected thread issues TMA loads: the Q tile once (3-D map
 //               over [s_q][n_heads][d]), then K and V tiles of 128 keys into
-//               two-stage rings (3-D maps over [n_kv_heads][keys][d]; zero fill
-//               past s_kv);
-//   warp 1      allocates TMEM (three 128-column S / P buffers and a D-column
-//               O accumulator) and one thread issues tcgen05.mma: S[j] = Q K[j]^T
-//               into buffer j % 3 (A = Q, B = K, both K-major, M = N = 128), then
-//               O += P[j-1] V[j-1] with A = P[j-1] read from tensor memory and
-//               B = V (MN-major, N = d), so the scores of tile j are formed while
-//               the softmax of tile j-1 runs; S[j] waits only for the PV product
-//               that last read its buffer (tile j-3);
+//               rings of ST stages (3-D maps over [n_kv_heads][keys][d]; zero
+//               fill past s_kv);
+//   warp 1      allocates TMEM (NB 128-column S / P buffers and a D-column O
+//               accumulator) and one thread issues tcgen05.mma: S[j] = Q K[j]^T
+//               into buffer j % NB (A = Q, B = K, both K-major, M = N = 128), and
+//               O += P[j] V[j] with A = P[j] read from tensor memory and B = V
+//               (MN-major, N = d); S[j] waits for the PV product that last read
+//               its buffer (tile j - NB);
 //   warps 2..   the softmax, NS threads per query row: warp w reads TMEM lanes
 //               32*(w%4)..+31 (its rows) and column group (w-2)/4 of them, so
 //               NS warps share each lane quarter (the MUFU and FMA work of a
@@ -70,21 +73,29 @@ constexpr float kAtRescale = 8.0f;
 #define ENGINE_ATTN_NS64 2
 #endif
 constexpr int kAtSplit128 = ENGINE_ATTN_NS128;  // softmax threads per row, d = 128
-constexpr int kAtSplit64 = ENGINE_ATTN_NS64;    // d = 64  // base-2 growth of a row max that triggers rescaling
+constexpr int kAtSplit64 = ENGINE_ATTN_NS64;    // d = 64
+#ifndef ENGINE_ATTN_BUFS
+#define ENGINE_ATTN_BUFS 1
+#endif
+constexpr int kAtBufs = ENGINE_ATTN_BUFS;       // S / P buffers (3: one CTA per SM, 1: two)
 
-template <int D>
+// NB S / P buffers in TMEM: 3 with one CTA per SM (two-stage K / V rings); 1
+// with two CTAs per SM (single K / V stages, 96 KB of shared memory and 256
+// TMEM columns each), whose serial S -> softmax -> PV chains interleave.
+template <int D, int NB>
 struct AtCfg {
   static constexpr int kDH = D / 64;                     // 64-wide (128-byte) column blocks
   static constexpr int kQBytes = kAtBM * D * 2;
   static constexpr int kKBytes = kAtBN * D * 2;
   static constexpr int kVBytes = kAtBN * D * 2;
-  static constexpr int kStages = 2;
+  static constexpr int kStages = NB == 3 ? 2 : 1;
   static constexpr int kOffK = kQBytes;
   static constexpr int kOffV = kOffK + kStages * kKBytes;
   static constexpr int kOffBar = kOffV + kStages * kVBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
-  static constexpr int kTmemCols = 512;  // S / P buffers 0-2 (128 columns each), O (D)
-  static constexpr int kOCol = 3 * kAtBN;
+  static constexpr int kTmemCols = NB == 3 ? 512 : 256;  // NB S / P buffers of 128 columns, O (D)
+  static constexpr int kOCol = NB * kAtBN;
+  static_assert(kOCol + D <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -115,12 +126,13 @@ __device__ __forceinline__ int64_t at_last_key(const AtParams& p, int64_t row) {
   return lim;
 }
 
-template <int D, int NS>
-__global__ void __launch_bounds__(at_threads(NS), 1)
+template <int D, int NS, int NB>
+__global__ void __launch_bounds__(at_threads(NS), NB == 3 ? 1 : 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AtParams p) {
-  using Cfg = AtCfg<D>;
+  using Cfg = AtCfg<D, NB>;
   constexpr int ST = Cfg::kStages;
+  static_assert(NB == 1 || NB == 3, "one or three S / P buffers");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -133,9 +145,9 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
   uint64_t* k_empty = k_full + ST;  // ST
   uint64_t* v_full = k_empty + ST;  // ST
   uint64_t* v_empty = v_full + ST;  // ST
-  uint64_t* s_full = v_empty + ST;  // 3: S(j) in buffer j % 3 complete
-  uint64_t* p_full = s_full + 3;    // 3: P(j) written over it
-  uint64_t* o_done = p_full + 3;    // 3: PV(j) complete
+  uint64_t* s_full = v_empty + ST;  // NB: S(j) in buffer j % NB complete
+  uint64_t* p_full = s_full + 3;    // NB: P(j) written over it
+  uint64_t* o_done = p_full + 3;    // NB: PV(j) complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 3);
   static_assert(kAtBN % (32 * NS) == 0 && D % (32 * NS) == 0, "column groups of 32");
   __shared__ float s_mx[2][NS][kAtBM];  // per-row exchange of the column groups' maxima
@@ -162,7 +174,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int b = 0; b < 3; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128 * NS);
       mbar_init(&o_done[b], 1);
@@ -236,9 +248,9 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       bool ok = mbar_wait(q_full, 0, p.limit_ns, p.err);
       const uint32_t q_addr = smem_u32(sQ);
       auto pv = [&](int i) {  // O += P[i] V[i], P[i] in TMEM over S[i]
-        const int b = i % 3;
+        const int b = i % NB;
         const int s = i % ST;
-        if (!mbar_wait(&p_full[b], (i / 3) & 1u, p.limit_ns, p.err)) return false;
+        if (!mbar_wait(&p_full[b], (i / NB) & 1u, p.limit_ns, p.err)) return false;
         if (!mbar_wait(&v_full[s], (i / ST) & 1u, p.limit_ns, p.err)) return false;
         tc_fence_after();
         const uint32_t pa = tmem_base + b * kAtBN;
@@ -256,13 +268,20 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       int last_s = -1, last_pv = -1;  // last S / PV products issued
       for (int j = 0; ok && j < ntiles; ++j) {
         const int s = j % ST;
-        const int b = j % 3;
+        const int b = j % NB;
         if (!mbar_wait(&k_full[s], (j / ST) & 1u, p.limit_ns, p.err)) {
           ok = false;
           break;
         }
-        // Buffer b last held P(j-3): its PV product must have read it.
-        if (j >= 3 && !mbar_wait(&o_done[b], ((j - 3) / 3) & 1u, p.limit_ns, p.err)) {
+        if (NB == 1 && j >= 1) {  // one buffer: PV(j-1) reads it before S(j) overwrites
+          if (pv(j - 1)) last_pv = j - 1;
+          else {
+            ok = false;
+            break;
+          }
+        }
+        // Buffer b last held P(j-NB): its PV product must have read it.
+        if (j >= NB && !mbar_wait(&o_done[b], ((j - NB) / NB) & 1u, p.limit_ns, p.err)) {
           ok = false;
           break;
         }
@@ -278,7 +297,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
         umma_commit(&k_empty[s]);
         umma_commit(&s_full[b]);
         last_s = j;
-        if (j >= 1) {
+        if (NB > 1 && j >= 1) {
           if (pv(j - 1)) last_pv = j - 1;
           else ok = false;
         }
@@ -288,9 +307,9 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       // commit arrives once every earlier MMA completed, so wait (bounded) for
       // the later of the last two commits.
       if (last_pv >= 0 && last_pv >= last_s) {
-        mbar_wait(&o_done[last_pv % 3], (last_pv / 3) & 1u, p.limit_ns, p.err);
+        mbar_wait(&o_done[last_pv % NB], (last_pv / NB) & 1u, p.limit_ns, p.err);
       } else if (last_s >= 0) {
-        mbar_wait(&s_full[last_s % 3], (last_s / 3) & 1u, p.limit_ns, p.err);
+        mbar_wait(&s_full[last_s % NB], (last_s / NB) & 1u, p.limit_ns, p.err);
       }
     }
     __syncwarp();
@@ -314,8 +333,8 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;   // parity of the max exchange
-      const int b3 = j % 3;  // S / P buffer
-      bool w = mbar_wait_sleepy(&s_full[b3], (j / 3) & 1u, p.limit_ns, p.err);
+      const int b3 = j % NB;  // S / P buffer
+      bool w = mbar_wait_sleepy(&s_full[b3], (j / NB) & 1u, p.limit_ns, p.err);
       if (!__all_sync(0xffffffffu, w)) {
         ok = false;
         break;
@@ -399,7 +418,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
       if (any_rescale) {
         if (j >= 1) {
-          w = mbar_wait_sleepy(&o_done[(j - 1) % 3], ((j - 1) / 3) & 1u, p.limit_ns, p.err);
+          w = mbar_wait_sleepy(&o_done[(j - 1) % NB], ((j - 1) / NB) & 1u, p.limit_ns, p.err);
           if (!__all_sync(0xffffffffu, w)) {
             ok = false;
             break;
@@ -431,7 +450,7 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
     }
     if (ok) {
       const int last = ntiles - 1;
-      const bool w = mbar_wait_sleepy(&o_done[last % 3], (last / 3) & 1u, p.limit_ns, p.err);
+      const bool w = mbar_wait_sleepy(&o_done[last % NB], (last / NB) & 1u, p.limit_ns, p.err);
       if (__all_sync(0xffffffffu, w)) {
         tc_fence_after();
         const float inv = 1.0f / l;
@@ -472,11 +491,11 @@ __global__ void __launch_bounds__(at_threads(NS), 1)
   }
 }
 
-template <int D, int NS>
+template <int D, int NS, int NB>
 int launch_attn_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                    const AtParams& p, cudaStream_t stream) {
-  using Cfg = AtCfg<D>;
-  auto kern = attn_tc_kernel<D, NS>;
+  using Cfg = AtCfg<D, NB>;
+  auto kern = attn_tc_kernel<D, NS, NB>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   B200_CUDA(cudaGetDevice(&dev));
@@ -530,8 +549,8 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
   p.c = scale * 1.4426950408889634f;
   p.err = device_error_word();
   p.limit_ns = wait_limit_ns();
-  const int rc = (d == 64) ? launch_attn_tc<64, kAtSplit64>(tq, tk, tv, p, stream)
-                           : launch_attn_tc<128, kAtSplit128>(tq, tk, tv, p, stream);
+  const int rc = (d == 64) ? launch_attn_tc<64, kAtSplit64, kAtBufs>(tq, tk, tv, p, stream)
+                           : launch_attn_tc<128, kAtSplit128, kAtBufs>(tq, tk, tv, p, stream);
   if (rc != ENGINE_OK) return rc;
   return check_launch("attention_prefill");
 }
