@@ -7,19 +7,23 @@
 // query head h reading KV head h / (n_heads / n_kv_heads).  Query row i sees
 // keys j <= q_pos_offset + i when causal, every key otherwise.
 //
-// One kernel serves both entry points.  A CTA takes one query position, up to
-// four query heads of one KV group and one split of the key range:
-// - Its 4 warps stream that KV head's K and V rows of the split with 16-byte
-//   loads (d / 8 lanes per key row), shared by the CTA's query heads, so K and V
-//   cross HBM once per split -- the decode bound.
-// - Each group of d / 8 lanes runs an FP32 online softmax over its keys: the
-//   running max m, sum l and the lane's 8 elements of the output accumulator.
-// - The CTA merges its lane groups in fixed order through shared memory; a
-//   single split writes out (and lse) directly, more splits write (m, l, O) to
-//   a workspace that attn_merge_kernel combines in split order.
-// Decode (one query position) gets enough splits to fill the GPU.  Prefill runs
-// the same kernel per query position: a correctness baseline for the engine's
-// prefill API; the tensor-core FlashAttention-2 prefill is the next step.
+// Dispatch (run_attention and the two entry points at the end of this file):
+// - attention_prefill from 16 query rows: the tcgen05 FlashAttention kernel in
+//   attention_tc.cu;
+// - attention_decode (and a one-row non-causal prefill) with head_dim 128, at
+//   most 16 query heads per KV head and automatic splits: the tcgen05 decode
+//   kernel in attention_tc.cu, its splits combined by attn_merge_kernel below;
+// - other decode shapes and explicit split counts: attn_decode_bulk_kernel
+//   below (K / V blocks by cp.async.bulk, CUDA-core arithmetic);
+// - everything else (a few query rows, unaligned strides): attn_split_kernel,
+//   the CUDA-core baseline.  A CTA takes one query position, up to four query
+//   heads of one KV group and one split of the key range; its 4 warps stream
+//   that KV head's K and V rows with 16-byte loads (d / 8 lanes per key row),
+//   each lane group runs an FP32 online softmax over its keys, the CTA merges
+//   its lane groups in fixed order through shared memory, and a single split
+//   writes out (and lse) directly while more splits write (m, l, O) to a
+//   workspace that attn_merge_kernel combines in split order.
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -576,6 +580,42 @@ int run_attention(const __half* q, const __half* k, const __half* v, __half* out
   const bool bulk = s_q == 1 && !causal && stride % 8 == 0 &&
                     ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) % 16) == 0;
+  static const int dec_tc_env = env_flag("ENGINE_ATTN_DECODE_TC", 1);
+  if (bulk && split_kv <= 0 && dec_tc_env != 0 && d == 128 && group <= 16 && scale > 0.0f) {
+    // tcgen05 decode (attention_tc.cu): splits of whole 128-key blocks, about
+    // two CTAs per SM (single-stage K / V rings: 77 KB of shared memory each).
+    static const int cps_env = env_flag("ENGINE_ATTN_DECODE_CPS", 2);
+    static const int nst_env = env_flag("ENGINE_ATTN_DECODE_NST", 1);
+    const int64_t want_tc =
+        std::max<int64_t>(1, (static_cast<int64_t>(cps_env) * sm_count()) / n_kv_heads);
+    int64_t chunk = (s_kv + want_tc - 1) / want_tc;
+    chunk = (chunk + 127) / 128 * 128;
+    const int64_t sp = (s_kv + chunk - 1) / chunk;
+    if (sp <= 65535) {
+      float* wst = nullptr;
+      if (sp > 1) {
+        const size_t bytes = static_cast<size_t>(n_heads) * sp * (d + 2) * sizeof(float);
+        wst = static_cast<float*>(scratch_alloc(bytes, st));
+        if (wst == nullptr)
+          return set_error(ENGINE_ERR_CUDA, std::string(what) + ": workspace allocation failed");
+      }
+      int rc = attention_decode_tc(q, k, v, out, lse, wst, s_kv, n_heads, n_kv_heads, d, stride,
+                                   scale, static_cast<int>(sp), chunk, nst_env == 2 ? 2 : 1, st);
+      if (rc == ENGINE_OK && sp > 1) {
+        a.ws = wst;
+        a.splits = static_cast<int>(sp);
+        a.chunk = chunk;
+        const cudaError_t e = launch_pdl(attn_merge_kernel<128>, dim3(static_cast<unsigned>(n_heads)),
+                                         dim3(kMergeWarps * 32), 0, st, a);
+        if (e != cudaSuccess) rc = set_cuda_error(e, "attn_merge_kernel");
+      }
+      if (wst != nullptr) scratch_free(wst, st);
+      if (rc != ENGINE_ERR_UNSUPPORTED) {
+        if (rc != ENGINE_OK) return rc;
+        return check_launch(what);
+      }
+    }
+  }
   int64_t splits = split_kv;
   if (splits <= 0 && bulk) {
     // decode: at least about four CTAs per SM, each split a whole number of

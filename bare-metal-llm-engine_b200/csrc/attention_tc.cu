@@ -510,6 +510,397 @@ int launch_attn_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   return ENGINE_OK;
 }
 
+// ---------------------------------------------------------------- decode
+//
+// attention_decode (one query position, non-causal) on tcgen05.  A CTA takes
+// one KV head and one split of its keys, in blocks of 128 keys, and serves the
+// G <= 16 query heads of that KV group together.  The products are formed
+// transposed, so that the 128 keys of a block (and later the d = 128 output
+// elements) fill the MMA's M = 128 rows:
+//   S^T[key, h] = K[key, :] . q[h, :]      A = K block (TMA, K-major), B = q^T
+//                                           (16 rows: the group's heads, the
+//                                           rows past them never used), N = 16
+//   O^T[e, h] += sum_key V[key, e] P[h, key]  A = V block as an MN-major operand
+//                                           (TMA), B = P^T written to shared
+//                                           memory by the softmax, N = 16
+// Warp 0 issues the TMA loads (q once, K / V blocks into nst-stage rings),
+// warp 1 owns TMEM (two 16-column S^T buffers and the O^T accumulator) and
+// issues the MMAs, warps 2-5 run the softmax: thread t holds key t of the
+// block (TMEM lane t) for all heads, takes each head's block maximum across
+// the 128 threads (warp shuffles, then a bounded mbarrier exchange), keeps the
+// running max m_h (base 2) with the lazy 2^8 rescaling of the prefill kernel,
+// writes P = exp2(S c - m_h) as FP16 into the swizzled P^T tile and keeps its
+// own partial sums l_h.  At the end thread e holds O^T[e, :] (TMEM lane e).  A
+// split writes (m ln 2, l, O) per head to the workspace that attn_merge_kernel
+// combines in split order; a single split writes out and lse directly.
+constexpr int kDtBlock = 128;  // keys per block
+constexpr int kDtN = 16;       // MMA N: query heads of one KV group, padded
+constexpr int kDtThreads = 192;
+
+struct DtParams {
+  __half* out;
+  float* lse;
+  float* ws;  // [n_heads][splits][D + 2]
+  int64_t s_kv, n_heads, group;
+  int64_t chunk;  // keys per split (a multiple of kDtBlock)
+  int splits;
+  int nst;        // K / V ring stages
+  float c;        // scale * log2(e)
+  unsigned int* err;
+  unsigned long long limit_ns;
+};
+
+template <int D>
+struct DtCfg {
+  static constexpr int kQBytes = kDtN * D * 2;          // 4 KB
+  static constexpr int kKBytes = kDtBlock * D * 2;      // 32 KB
+  static constexpr int kPBytes = kDtN * kDtBlock * 2;   // 4 KB
+  static constexpr int smem(int nst) { return kQBytes + 2 * kPBytes + nst * 2 * kKBytes + 256 + 1024; }
+};
+
+template <int D, bool FINAL>
+__global__ void __launch_bounds__(kDtThreads)
+    attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const DtParams p) {
+  using Cfg = DtCfg<D>;
+  static_assert(D == 128, "the O^T product uses M = d = 128");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int nst = p.nst;
+  uint8_t* sQ = smem;
+  uint8_t* sP = smem + Cfg::kQBytes;                    // two P^T tiles
+  uint8_t* sK = sP + 2 * Cfg::kPBytes;                  // nst stages
+  uint8_t* sV = sK + nst * Cfg::kKBytes;                // nst stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + nst * Cfg::kKBytes);
+  uint64_t* q_full = bars;           // 1
+  uint64_t* k_full = bars + 1;       // 2 (nst <= 2)
+  uint64_t* k_empty = k_full + 2;
+  uint64_t* v_full = k_empty + 2;
+  uint64_t* v_empty = v_full + 2;
+  uint64_t* s_full = v_empty + 2;    // 2
+  uint64_t* p_full = s_full + 2;     // 2
+  uint64_t* o_done = p_full + 2;     // 2
+  uint64_t* xbar = o_done + 2;       // 2: the block-max exchange, by parity
+  uint64_t* lbar = xbar + 2;         // 1: the final sums
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lbar + 1);
+  __shared__ float s_mx[2][4][kDtN];
+  __shared__ float s_l[4][kDtN];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int hk = blockIdx.y;
+  const int64_t h0 = static_cast<int64_t>(hk) * p.group;  // first query head of the group
+  const int G = static_cast<int>(p.group);
+  const int64_t j0 = static_cast<int64_t>(split) * p.chunk;
+  const int64_t j1 = (j0 + p.chunk < p.s_kv) ? j0 + p.chunk : p.s_kv;
+  const int nblk = j1 > j0 ? static_cast<int>((j1 - j0 + kDtBlock - 1) / kDtBlock) : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
+      mbar_init(&xbar[s], 128);
+    }
+    mbar_init(lbar, 128);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 64);
+    tmem_relinquish();
+  }
+  if (warp >= 2) {  // the P^T rows past the group's heads stay zero
+    for (int i = threadIdx.x - 64; i < 2 * Cfg::kPBytes / 16; i += 128)
+      reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
+#pragma unroll
+      for (int dh = 0; dh < D / 64; ++dh)
+        tma_load_2d(sQ + dh * (kDtN * 128), &tmQ, q_full, dh * 64, static_cast<int32_t>(h0));
+      int kn = 0, vn = 0;
+      for (int b = 0; b < nblk; ++b) {
+        const int s = b % nst;
+        const uint32_t ph = (b / nst) & 1u;
+        const int32_t jb = static_cast<int32_t>(j0 + static_cast<int64_t>(b) * kDtBlock);
+        if (!mbar_wait(&k_empty[s], ph ^ 1u, p.limit_ns, p.err)) break;
+        mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
+#pragma unroll
+        for (int dh = 0; dh < D / 64; ++dh)
+          tma_load_3d(sK + s * Cfg::kKBytes + dh * 16384, &tmK, &k_full[s], dh * 64, jb, hk);
+        ++kn;
+        if (!mbar_wait(&v_empty[s], ph ^ 1u, p.limit_ns, p.err)) break;
+        mbar_arrive_expect_tx(&v_full[s], Cfg::kKBytes);
+#pragma unroll
+        for (int kh = 0; kh < 2; ++kh) {
+#pragma unroll
+          for (int dh = 0; dh < D / 64; ++dh)
+            tma_load_3d(sV + s * Cfg::kKBytes + kh * (D / 64) * 8192 + dh * 8192, &tmV, &v_full[s],
+                        dh * 64, jb + kh * 64, hk);
+        }
+        ++vn;
+      }
+      mbar_wait(q_full, 0, p.limit_ns, p.err);
+      for (int b = (kn > nst ? kn - nst : 0); b < kn; ++b)
+        mbar_wait(&k_full[b % nst], (b / nst) & 1u, p.limit_ns, p.err);
+      for (int b = (vn > nst ? vn - nst : 0); b < vn; ++b)
+        mbar_wait(&v_full[b % nst], (b / nst) & 1u, p.limit_ns, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t kIdescS = umma_idesc_f16(128, kDtN, false, false, false);
+      constexpr uint32_t kIdescO = umma_idesc_f16(128, kDtN, false, true, false);
+      const uint32_t tO = tmem_base + 32;
+      bool ok = mbar_wait(q_full, 0, p.limit_ns, p.err);
+      const uint32_t q_addr = smem_u32(sQ);
+      int last_s = -1, last_pv = -1;
+      auto pv = [&](int i) {  // O^T += V[i]^T P[i]^T
+        const int s = i % nst;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1u, p.limit_ns, p.err)) return false;
+        if (!mbar_wait(&v_full[s], (i / nst) & 1u, p.limit_ns, p.err)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_u32(sV + s * Cfg::kKBytes);
+        const uint32_t pa = smem_u32(sP + (i & 1) * Cfg::kPBytes);
+#pragma unroll
+        for (int kk = 0; kk < kDtBlock / 16; ++kk) {
+          const uint64_t adesc =
+              umma_desc_sw128(va + (kk >> 2) * ((D / 64) * 8192) + (kk & 3) * 2048, 8192, 1024);
+          const uint64_t bdesc = umma_desc_sw128(pa + (kk >> 2) * (kDtN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_f16(tO, adesc, bdesc, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&v_empty[s]);
+        umma_commit(&o_done[i & 1]);
+        last_pv = i;
+        return true;
+      };
+      for (int b = 0; ok && b < nblk; ++b) {
+        const int s = b % nst;
+        if (!mbar_wait(&k_full[s], (b / nst) & 1u, p.limit_ns, p.err)) break;
+        // S^T buffer b & 1 was last read by the softmax of block b - 2, which
+        // finished before P(b-2) was released: PV(b-2) has been issued after it.
+        if (b >= 2 && !mbar_wait(&p_full[b & 1], ((b - 2) >> 1) & 1u, p.limit_ns, p.err)) break;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + s * Cfg::kKBytes);
+        const uint32_t tS = tmem_base + (b & 1) * kDtN;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t adesc = umma_desc_sw128(ka + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = umma_desc_sw128(q_addr + (kk >> 2) * (kDtN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_f16(tS, adesc, bdesc, kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&k_empty[s]);
+        umma_commit(&s_full[b & 1]);
+        last_s = b;
+        if (b >= 1 && !pv(b - 1)) ok = false;
+      }
+      if (ok && nblk > 0) pv(nblk - 1);
+      if (last_pv >= 0 && last_pv >= last_s) {
+        mbar_wait(&o_done[last_pv & 1], (last_pv >> 1) & 1u, p.limit_ns, p.err);
+      } else if (last_s >= 0) {
+        mbar_wait(&s_full[last_s & 1], (last_s >> 1) & 1u, p.limit_ns, p.err);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int t = q4 * 32 + lane;  // key of the block / output element
+    const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
+    float m[kDtN], l[kDtN];
+#pragma unroll
+    for (int h = 0; h < kDtN; ++h) {
+      m[h] = -INFINITY;
+      l[h] = 0.0f;
+    }
+    bool ok = true;
+    for (int b = 0; b < nblk; ++b) {
+      const int bb = b & 1;
+      bool w = mbar_wait_sleepy(&s_full[bb], (b >> 1) & 1u, p.limit_ns, p.err);
+      if (!__all_sync(0xffffffffu, w)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[kDtN];
+      tmem_ld_32x32b_x16(tmem_base + lane_base + bb * kDtN, sv);
+      tmem_wait_ld();
+      const int64_t key = j0 + static_cast<int64_t>(b) * kDtBlock + t;
+      const bool valid = key < j1;
+      float x[kDtN], mx[kDtN];
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        x[h] = valid ? __uint_as_float(sv[h]) : -INFINITY;
+        mx[h] = x[h];
+      }
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        if (h < G) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], o));
+        }
+      }
+      if (lane < kDtN) {
+        float v = mx[0];
+#pragma unroll
+        for (int h = 1; h < kDtN; ++h) v = (lane == h) ? mx[h] : v;
+        s_mx[bb][q4][lane] = v;
+      }
+      mbar_arrive(&xbar[bb]);
+      w = mbar_wait_sleepy(&xbar[bb], (b >> 1) & 1u, p.limit_ns, p.err);
+      if (!__all_sync(0xffffffffu, w)) {
+        ok = false;
+        break;
+      }
+      // P^T tile bb is free once PV(b-2) completed; O may be rescaled only once
+      // PV(b-1) completed (PV(b) waits for this block's p_full).
+      bool rescale_any = false;
+      float alpha[kDtN], base[kDtN];
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        const float bm = fmaxf(fmaxf(s_mx[bb][0][h], s_mx[bb][1][h]),
+                               fmaxf(s_mx[bb][2][h], s_mx[bb][3][h])) * p.c;
+        const bool first = (m[h] == -INFINITY);
+        const bool rs = !first && bm > m[h] + kAtRescale;
+        const float mn = (first || rs) ? fmaxf(m[h], bm) : m[h];
+        base[h] = (mn == -INFINITY) ? 0.0f : mn;
+        alpha[h] = ex2_fast(m[h] - base[h]);
+        rescale_any |= (h < G) && rs;
+        m[h] = mn;
+      }
+      const int dep = rescale_any ? b - 1 : b - 2;
+      if (dep >= 0) {
+        w = mbar_wait_sleepy(&o_done[dep & 1], (dep >> 1) & 1u, p.limit_ns, p.err);
+        if (!__all_sync(0xffffffffu, w)) {
+          ok = false;
+          break;
+        }
+      }
+      // P^T[h][t]: row h (128 bytes per 64 keys), 16-byte chunk (t % 64) / 8
+      // swizzled by h % 8, element t % 8.
+      uint8_t* pt = sP + bb * Cfg::kPBytes + (t >> 6) * (kDtN * 128);
+      const int chunk = (t & 63) >> 3;
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        if (h < G) {
+          const float pv = ex2_fast(fmaf(x[h], p.c, -base[h]));
+          l[h] = l[h] * alpha[h] + pv;
+          *reinterpret_cast<__half*>(pt + h * 128 + ((chunk ^ (h & 7)) << 4) + (t & 7) * 2) =
+              __float2half_rn(pv);
+        }
+      }
+      if (rescale_any) {  // thread t owns output element t of every head (TMEM lane t)
+        tc_fence_after();
+        uint32_t ov[kDtN];
+        tmem_ld_32x32b_x16(tmem_base + lane_base + 32, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < kDtN; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * alpha[h]);
+        tmem_st_32x32b_x16(tmem_base + lane_base + 32, ov);
+        tmem_wait_st();
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[bb]);
+    }
+    // Per-head sums over the 128 threads, then the output.
+    if (ok) {
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        if (h < G) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) l[h] += __shfl_xor_sync(0xffffffffu, l[h], o);
+        }
+      }
+      if (lane < kDtN) {
+        float v = l[0];
+#pragma unroll
+        for (int h = 1; h < kDtN; ++h) v = (lane == h) ? l[h] : v;
+        s_l[q4][lane] = v;
+      }
+      mbar_arrive(lbar);
+      ok = __all_sync(0xffffffffu, mbar_wait_sleepy(lbar, 0, p.limit_ns, p.err));
+    }
+    if (ok && nblk > 0) {
+      const int last = nblk - 1;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait_sleepy(&o_done[last & 1], (last >> 1) & 1u, p.limit_ns, p.err));
+    }
+    if (ok) {
+      uint32_t ov[kDtN];
+      if (nblk > 0) {
+        tc_fence_after();
+        tmem_ld_32x32b_x16(tmem_base + lane_base + 32, ov);
+        tmem_wait_ld();
+      }
+#pragma unroll
+      for (int h = 0; h < kDtN; ++h) {
+        if (h >= G) continue;
+        const float L = (s_l[0][h] + s_l[1][h]) + (s_l[2][h] + s_l[3][h]);
+        const float o = nblk > 0 ? __uint_as_float(ov[h]) : 0.0f;
+        const int64_t row = h0 + h;
+        const float mnat = (nblk > 0 && m[h] != -INFINITY) ? m[h] * 0.69314718055994531f : -INFINITY;
+        if constexpr (FINAL) {
+          p.out[row * D + t] = __float2half_rn(L > 0.0f ? o / L : 0.0f);
+          if (t == 0 && p.lse != nullptr) p.lse[row] = L > 0.0f ? mnat + logf(L) : -INFINITY;
+        } else {
+          float* wsr = p.ws + (row * p.splits + split) * (D + 2);
+          if (t == 0) {
+            wsr[0] = mnat;
+            wsr[1] = L;
+          }
+          wsr[2 + t] = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 64);
+  }
+}
+
+template <int D, bool FINAL>
+int launch_decode_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const DtParams& p, unsigned n_kv_heads, cudaStream_t stream) {
+  auto kern = attn_decode_tc_kernel<D, FINAL>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  B200_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((configured.load() & bit) == 0) {
+    B200_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   DtCfg<D>::smem(2)));
+    configured.fetch_or(bit);
+  }
+  B200_CUDA(launch_pdl(kern, dim3(static_cast<unsigned>(p.splits), n_kv_heads), dim3(kDtThreads),
+                       static_cast<size_t>(DtCfg<D>::smem(p.nst)), stream, tq, tk, tv, p));
+  return ENGINE_OK;
+}
+
 }  // namespace
 
 int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __half* out,
@@ -553,6 +944,52 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
                            : launch_attn_tc<128, kAtSplit128, kAtBufs>(tq, tk, tv, p, stream);
   if (rc != ENGINE_OK) return rc;
   return check_launch("attention_prefill");
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+int attention_decode_tc(const __half* q, const __half* k, const __half* v, __half* out, float* lse,
+                        float* ws, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
+                        int64_t kv_head_stride, float scale, int splits, int64_t chunk,
+                        int nst, cudaStream_t stream) {
+  const int64_t group = n_kv_heads > 0 ? n_heads / n_kv_heads : 0;
+  if (d != 128 || group < 1 || group > kDtN || !(scale > 0.0f) || kv_head_stride % 8 != 0 ||
+      chunk % kDtBlock != 0 || splits < 1 || (splits > 1 && ws == nullptr) ||
+      s_kv > (int64_t{1} << 31) || n_kv_heads > 65535 ||
+      (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+       reinterpret_cast<uintptr_t>(v)) % 16 != 0)
+    return ENGINE_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  const uint64_t kd[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(s_kv),
+                          static_cast<uint64_t>(n_kv_heads)};
+  const uint64_t ks[2] = {static_cast<uint64_t>(d), static_cast<uint64_t>(kv_head_stride)};
+  const uint32_t kbox[3] = {64, kDtBlock, 1};
+  const uint32_t vbox[3] = {64, 64, 1};
+  if (!make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<uint64_t>(n_heads),
+                    static_cast<uint64_t>(d), static_cast<uint64_t>(d), kDtN, 64) ||
+      !make_tmap_3d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kd, ks, kbox) ||
+      !make_tmap_3d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kd, ks, vbox))
+    return ENGINE_ERR_UNSUPPORTED;
+  DtParams p{};
+  p.out = out;
+  p.lse = lse;
+  p.ws = ws;
+  p.s_kv = s_kv;
+  p.n_heads = n_heads;
+  p.group = group;
+  p.chunk = chunk;
+  p.splits = splits;
+  p.nst = (chunk > kDtBlock && nst == 2) ? 2 : 1;
+  p.c = scale * 1.4426950408889634f;
+  p.err = device_error_word();
+  p.limit_ns = wait_limit_ns();
+  const unsigned hk = static_cast<unsigned>(n_kv_heads);
+  const int rc = splits == 1 ? launch_decode_tc<128, true>(tq, tk, tv, p, hk, stream)
+                             : launch_decode_tc<128, false>(tq, tk, tv, p, hk, stream);
+  if (rc != ENGINE_OK) return rc;
+  return check_launch("attention_decode");
 }
 
 }  // namespace b200

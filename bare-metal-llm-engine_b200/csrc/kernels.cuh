@@ -72,6 +72,18 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
                          int64_t kv_head_stride, float scale, int64_t q_pos_offset, bool causal,
                          float* lse, cudaStream_t stream);
 
+/// Attention decode on tcgen05 (attention_tc.cu): one query position, d = 128,
+/// up to 16 query heads per KV head; `splits` splits of `chunk` keys (a multiple
+/// of 128) per KV head, each writing (m, l, O) to ws[n_heads][splits][d + 2]
+/// for attn_merge_kernel, or out / lse directly when splits == 1; nst = 1 or 2
+/// K / V ring stages (1: 77 KB of shared memory, two CTAs per SM).  Returns
+/// ENGINE_ERR_UNSUPPORTED, with nothing launched, for shapes or alignments it
+/// does not take.
+int attention_decode_tc(const __half* q, const __half* k, const __half* v, __half* out, float* lse,
+                        float* ws, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
+                        int64_t kv_head_stride, float scale, int splits, int64_t chunk,
+                        int nst, cudaStream_t stream);
+
 /// Zeroes the stream-K tile counters of every workspace on `dev` (after a
 /// device-side time-out may have left a launch half counted).  The device must
 /// be idle.  gemm_tc.cu.
