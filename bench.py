@@ -454,6 +454,32 @@ def secondary_configs(torch, pkg, dev, g, world, args, local=0):
         del X, Y, sets
     del Ws
     torch.cuda.empty_cache()
+    # Attention (the engine's attention_prefill / attention_decode launchers),
+    # Llama-3-8B heads (32 query, 8 KV, d = 128): causal prefill at S = 2048
+    # (FLOPs of the causal half: 2 * S^2 * d * heads), and decode of one token
+    # over 4096 and 16384 cached keys (bytes: K and V once).
+    H, Hk, d = 32, 8, 128
+    S = 2048
+    sets = [(torch.randn(S, H, d, device=dev, generator=g).half(),
+             torch.randn(Hk, S, d, device=dev, generator=g).half(),
+             torch.randn(Hk, S, d, device=dev, generator=g).half(),
+             torch.empty(S, H, d, device=dev, dtype=torch.float16)) for _ in range(2)]
+    fn = lambda s, st: pkg.cuda.attention_prefill(  # noqa: E731
+        s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), s[3].data_ptr(), S, S, H, Hk, d, S * d,
+        d ** -0.5, 0, True, 0, st)
+    timed("attn_prefill_s2048", fn, sets, 20, 3, flops=2.0 * S * S * d * H)
+    del sets
+    for kv, nsets in ((4096, 10), (16384, 3)):
+        sets = [(torch.randn(H, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.empty(H, d, device=dev, dtype=torch.float16)) for _ in range(nsets)]
+        fn = lambda s, st, kv=kv: pkg.cuda.attention_decode(  # noqa: E731
+            s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(), s[3].data_ptr(), kv, H, Hk, d,
+            kv * d, d ** -0.5, 0, st)
+        timed(f"attn_decode_{kv}", fn, sets, 60, 5, byt=2.0 * 2 * Hk * kv * d)
+        del sets
+    torch.cuda.empty_cache()
     # The 14336x4096 GEMV again, right after the prefill GEMMs: the same kernel
     # and weights as the entry at the top of the sequence, so any difference in
     # "us" or "kcyc" is the GPU's state after long tensor-core work.
