@@ -12,7 +12,8 @@
 //   attention_tc.cu;
 // - attention_decode (and a one-row non-causal prefill) with head_dim 128, at
 //   most 16 query heads per KV head and automatic splits: the tcgen05 decode
-//   kernel in attention_tc.cu, its splits combined by attn_merge_kernel below;
+//   kernel in attention_tc.cu, its splits combined inside a thread-block
+//   cluster (up to 8 key blocks of 128 per KV head) or by attn_merge_kernel;
 // - other decode shapes and explicit split counts: attn_decode_bulk_kernel
 //   below (K / V blocks by cp.async.bulk, CUDA-core arithmetic);
 // - everything else (a few query rows, unaligned strides): attn_split_kernel,
@@ -581,40 +582,31 @@ int run_attention(const __half* q, const __half* k, const __half* v, __half* out
                     ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) % 16) == 0;
   static const int dec_tc_env = env_flag("ENGINE_ATTN_DECODE_TC", 1);
-  if (bulk && split_kv <= 0 && dec_tc_env != 0 && d == 128 && group <= 16 && scale > 0.0f) {
-    // tcgen05 decode (attention_tc.cu): splits of whole 128-key blocks, about
-    // two CTAs per SM (single-stage K / V rings: 77 KB of shared memory each).
-    static const int cps_env = env_flag("ENGINE_ATTN_DECODE_CPS", 2);
-    static const int nst_env = env_flag("ENGINE_ATTN_DECODE_NST", 1);
-    const int64_t want_tc =
-        std::max<int64_t>(1, (static_cast<int64_t>(cps_env) * sm_count()) / n_kv_heads);
-    int64_t chunk = (s_kv + want_tc - 1) / want_tc;
-    chunk = (chunk + 127) / 128 * 128;
-    const int64_t sp = (s_kv + chunk - 1) / chunk;
-    if (sp <= 65535) {
-      float* wst = nullptr;
-      if (sp > 1) {
-        const size_t bytes = static_cast<size_t>(n_heads) * sp * (d + 2) * sizeof(float);
-        wst = static_cast<float*>(scratch_alloc(bytes, st));
-        if (wst == nullptr)
-          return set_error(ENGINE_ERR_CUDA, std::string(what) + ": workspace allocation failed");
-      }
-      int rc = attention_decode_tc(q, k, v, out, lse, wst, s_kv, n_heads, n_kv_heads, d, stride,
-                                   scale, static_cast<int>(sp), chunk, nst_env == 2 ? 2 : 1, st);
-      if (rc == ENGINE_OK && sp > 1) {
-        a.ws = wst;
-        a.splits = static_cast<int>(sp);
-        a.chunk = chunk;
-        const cudaError_t e = launch_pdl(attn_merge_kernel<128>, dim3(static_cast<unsigned>(n_heads)),
-                                         dim3(kMergeWarps * 32), 0, st, a);
-        if (e != cudaSuccess) rc = set_cuda_error(e, "attn_merge_kernel");
-      }
-      if (wst != nullptr) scratch_free(wst, st);
-      if (rc != ENGINE_ERR_UNSUPPORTED) {
-        if (rc != ENGINE_OK) return rc;
-        return check_launch(what);
-      }
+  if (bulk && split_kv <= 0 && dec_tc_env != 0) {
+    // tcgen05 decode (attention_tc.cu), its splits merged inside one cluster per
+    // KV head; shapes it does not take fall through to the bulk kernel.
+    int64_t chunk = 0;
+    const int sp = attention_decode_tc_splits(s_kv, n_kv_heads, &chunk);
+    float* wst = nullptr;
+    if (sp > 1) {
+      const size_t bytes = static_cast<size_t>(n_heads) * sp * (d + 2) * sizeof(float);
+      wst = static_cast<float*>(scratch_alloc(bytes, st));
+      if (wst == nullptr)
+        return set_error(ENGINE_ERR_CUDA, std::string(what) + ": workspace allocation failed");
     }
+    int rc = attention_decode_tc(q, k, v, out, lse, wst, s_kv, n_heads, n_kv_heads, d, stride,
+                                 scale, st);
+    if (rc == ENGINE_OK && sp > 1) {
+      a.ws = wst;
+      a.splits = sp;
+      a.chunk = chunk;
+      const cudaError_t e = launch_pdl(attn_merge_kernel<128>, dim3(static_cast<unsigned>(n_heads)),
+                                       dim3(kMergeWarps * 32), 0, st, a);
+      if (e != cudaSuccess) rc = set_cuda_error(e, "attn_merge_kernel");
+      else rc = check_launch(what);
+    }
+    if (wst != nullptr) scratch_free(wst, st);
+    if (rc != ENGINE_ERR_UNSUPPORTED) return rc;
   }
   int64_t splits = split_kv;
   if (splits <= 0 && bulk) {

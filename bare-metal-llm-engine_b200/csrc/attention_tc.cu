@@ -51,7 +51,9 @@
 //
 // Every mbarrier wait is bounded (ENGINE_WAIT_TIMEOUT_MS): on expiry the thread
 // sets the device error word, abandons its loop and reaches the common teardown.
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cmath>
 
 #include "common.cuh"
@@ -531,8 +533,11 @@ int launch_attn_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
 // running max m_h (base 2) with the lazy 2^8 rescaling of the prefill kernel,
 // writes P = exp2(S c - m_h) as FP16 into the swizzled P^T tile and keeps its
 // own partial sums l_h.  At the end thread e holds O^T[e, :] (TMEM lane e).  A
-// split writes (m ln 2, l, O) per head to the workspace that attn_merge_kernel
-// combines in split order; a single split writes out and lse directly.
+// single split writes out and lse directly.  Otherwise the R <= 16 splits of a
+// KV head form one thread-block cluster: each CTA parks its (m, l, O) in its
+// own shared memory, and after a cluster barrier the CTAs combine them through
+// distributed shared memory (rank order, base 2) and write out and lse -- no
+// workspace and no second kernel.
 constexpr int kDtBlock = 128;  // keys per block
 constexpr int kDtN = 16;       // MMA N: query heads of one KV group, padded
 constexpr int kDtThreads = 192;
@@ -540,10 +545,10 @@ constexpr int kDtThreads = 192;
 struct DtParams {
   __half* out;
   float* lse;
-  float* ws;  // [n_heads][splits][D + 2]
+  float* ws;      // kDtWs: [n_heads][splits][D + 2], m (natural log), l, O
   int64_t s_kv, n_heads, group;
   int64_t chunk;  // keys per split (a multiple of kDtBlock)
-  int splits;
+  int splits;     // CTAs per KV head: the cluster size when > 1
   int nst;        // K / V ring stages
   float c;        // scale * log2(e)
   unsigned int* err;
@@ -558,7 +563,11 @@ struct DtCfg {
   static constexpr int smem(int nst) { return kQBytes + 2 * kPBytes + nst * 2 * kKBytes + 256 + 1024; }
 };
 
-template <int D, bool FINAL>
+// MODE: kDtFinal (one split: out and lse), kDtWs (splits to the workspace for
+// attn_merge_kernel), kDtCluster (splits merged inside the cluster).
+constexpr int kDtFinal = 0, kDtWs = 1, kDtCluster = 2;
+
+template <int D, int MODE>
 __global__ void __launch_bounds__(kDtThreads)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
@@ -861,19 +870,59 @@ __global__ void __launch_bounds__(kDtThreads)
         const float o = nblk > 0 ? __uint_as_float(ov[h]) : 0.0f;
         const int64_t row = h0 + h;
         const float mnat = (nblk > 0 && m[h] != -INFINITY) ? m[h] * 0.69314718055994531f : -INFINITY;
-        if constexpr (FINAL) {
+        if constexpr (MODE == kDtFinal) {
           p.out[row * D + t] = __float2half_rn(L > 0.0f ? o / L : 0.0f);
           if (t == 0 && p.lse != nullptr) p.lse[row] = L > 0.0f ? mnat + logf(L) : -INFINITY;
-        } else {
+        } else if constexpr (MODE == kDtWs) {
           float* wsr = p.ws + (row * p.splits + split) * (D + 2);
           if (t == 0) {
             wsr[0] = mnat;
             wsr[1] = L;
           }
           wsr[2 + t] = o;
+        } else {
+          // The partial for the cluster merge: O[h][e], then m[h] (base 2), l[h].
+          float* part = reinterpret_cast<float*>(sK);
+          part[h * D + t] = o;
+          if (t == 0) {
+            part[kDtN * D + h] = (nblk > 0) ? m[h] : -INFINITY;
+            part[kDtN * D + kDtN + h] = L;
+          }
         }
       }
     }
+  }
+  if constexpr (MODE == kDtCluster) {
+    // Every thread of every CTA reaches both cluster barriers (no early exit on
+    // any path; the waits above are bounded).  The first makes each CTA's
+    // partial visible cluster-wide; the second keeps every CTA resident until
+    // its partial has been read.
+    __syncwarp();
+    cluster_sync_all();
+    if (warp >= 2) {
+      const int t = (warp & 3) * 32 + lane;
+      const int R = p.splits;
+      const uint32_t rank = cluster_ctarank();
+      const uint32_t part = smem_u32(sK);
+      for (int idx = static_cast<int>(rank) * 128 + t; idx < G * D; idx += R * 128) {
+        const int h = idx / D, e = idx % D;
+        float M = -INFINITY;
+        for (int q = 0; q < R; ++q)
+          M = fmaxf(M, ld_dsmem_f32(mapa_shared(part + 4u * (kDtN * D + h), q)));
+        float Ls = 0.0f, Os = 0.0f;
+        for (int q = 0; q < R; ++q) {
+          const float mq = ld_dsmem_f32(mapa_shared(part + 4u * (kDtN * D + h), q));
+          const float wq = (mq == -INFINITY) ? 0.0f : ex2_fast(mq - M);
+          Ls = fmaf(ld_dsmem_f32(mapa_shared(part + 4u * (kDtN * D + kDtN + h), q)), wq, Ls);
+          Os = fmaf(ld_dsmem_f32(mapa_shared(part + 4u * (h * D + e), q)), wq, Os);
+        }
+        const int64_t row = h0 + h;
+        p.out[row * D + e] = __float2half_rn(Ls > 0.0f ? Os / Ls : 0.0f);
+        if (e == 0 && p.lse != nullptr)
+          p.lse[row] = Ls > 0.0f ? M * 0.69314718055994531f + logf(Ls) : -INFINITY;
+      }
+    }
+    cluster_sync_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -883,10 +932,33 @@ __global__ void __launch_bounds__(kDtThreads)
   }
 }
 
-template <int D, bool FINAL>
-int launch_decode_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     const DtParams& p, unsigned n_kv_heads, cudaStream_t stream) {
-  auto kern = attn_decode_tc_kernel<D, FINAL>;
+template <int D, int MODE>
+cudaLaunchConfig_t decode_tc_config(const DtParams& p, unsigned n_kv_heads, cudaStream_t stream,
+                                    cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.splits), n_kv_heads);
+  cfg.blockDim = dim3(kDtThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(DtCfg<D>::smem(p.nst));
+  cfg.stream = stream;
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  if (pdl_enabled()) ++n;
+  if (MODE == kDtCluster) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(p.splits);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cfg;
+}
+
+template <int D, int MODE>
+int configure_decode_tc() {
+  auto kern = attn_decode_tc_kernel<D, MODE>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   B200_CUDA(cudaGetDevice(&dev));
@@ -896,8 +968,6 @@ int launch_decode_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
                                    DtCfg<D>::smem(2)));
     configured.fetch_or(bit);
   }
-  B200_CUDA(launch_pdl(kern, dim3(static_cast<unsigned>(p.splits), n_kv_heads), dim3(kDtThreads),
-                       static_cast<size_t>(DtCfg<D>::smem(p.nst)), stream, tq, tk, tv, p));
   return ENGINE_OK;
 }
 
@@ -950,14 +1020,24 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
 
 namespace b200 {
 
+int attention_decode_tc_splits(int64_t s_kv, int64_t n_kv_heads, int64_t* chunk) {
+  const int64_t nblocks = (s_kv + kDtBlock - 1) / kDtBlock;
+  if (nblocks <= 8) {
+    *chunk = kDtBlock;
+    return 0;  // merged inside a cluster: no workspace
+  }
+  const int64_t want = std::max<int64_t>(1, (2 * static_cast<int64_t>(sm_count())) / n_kv_heads);
+  const int64_t bpc = (nblocks + want - 1) / want;  // blocks per split
+  *chunk = bpc * kDtBlock;
+  return static_cast<int>((nblocks + bpc - 1) / bpc);
+}
+
 int attention_decode_tc(const __half* q, const __half* k, const __half* v, __half* out, float* lse,
                         float* ws, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
-                        int64_t kv_head_stride, float scale, int splits, int64_t chunk,
-                        int nst, cudaStream_t stream) {
+                        int64_t kv_head_stride, float scale, cudaStream_t stream) {
   const int64_t group = n_kv_heads > 0 ? n_heads / n_kv_heads : 0;
   if (d != 128 || group < 1 || group > kDtN || !(scale > 0.0f) || kv_head_stride % 8 != 0 ||
-      chunk % kDtBlock != 0 || splits < 1 || (splits > 1 && ws == nullptr) ||
-      s_kv > (int64_t{1} << 31) || n_kv_heads > 65535 ||
+      s_kv < 1 || s_kv > (int64_t{1} << 31) || n_kv_heads > 65535 ||
       (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
        reinterpret_cast<uintptr_t>(v)) % 16 != 0)
     return ENGINE_ERR_UNSUPPORTED;
@@ -975,20 +1055,52 @@ int attention_decode_tc(const __half* q, const __half* k, const __half* v, __hal
   DtParams p{};
   p.out = out;
   p.lse = lse;
-  p.ws = ws;
   p.s_kv = s_kv;
   p.n_heads = n_heads;
   p.group = group;
-  p.chunk = chunk;
-  p.splits = splits;
-  p.nst = (chunk > kDtBlock && nst == 2) ? 2 : 1;
   p.c = scale * 1.4426950408889634f;
   p.err = device_error_word();
   p.limit_ns = wait_limit_ns();
+  // Splits of whole 128-key blocks.  Up to 8 blocks per KV head: one split per
+  // block, merged inside a cluster of at most 8 CTAs (portable size).  More:
+  // about two CTAs per SM over all heads (single-stage K / V rings, 79 KB of
+  // shared memory each), merged by attn_merge_kernel through the workspace.
+  // (Clusters of 16 cannot all be resident on B200 -- a GPC rarely has 16 free
+  // SMs -- and clusters of 8 leave half the SMs idle on long contexts.)
+  const int64_t nblocks = (s_kv + kDtBlock - 1) / kDtBlock;
   const unsigned hk = static_cast<unsigned>(n_kv_heads);
-  const int rc = splits == 1 ? launch_decode_tc<128, true>(tq, tk, tv, p, hk, stream)
-                             : launch_decode_tc<128, false>(tq, tk, tv, p, hk, stream);
-  if (rc != ENGINE_OK) return rc;
+  if (nblocks <= 8) {
+    p.splits = static_cast<int>(nblocks);
+    p.chunk = kDtBlock;
+    p.nst = 1;
+    cudaLaunchAttribute attr[2];
+    if (p.splits == 1) {
+      const int rc = configure_decode_tc<128, kDtFinal>();
+      if (rc != ENGINE_OK) return rc;
+      cudaLaunchConfig_t cfg = decode_tc_config<128, kDtFinal>(p, hk, stream, attr);
+      B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtFinal>, tq, tk, tv, p));
+    } else {
+      const int rc = configure_decode_tc<128, kDtCluster>();
+      if (rc != ENGINE_OK) return rc;
+      cudaLaunchConfig_t cfg = decode_tc_config<128, kDtCluster>(p, hk, stream, attr);
+      B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtCluster>, tq, tk, tv, p));
+    }
+    return check_launch("attention_decode");
+  }
+  if (ws == nullptr) return ENGINE_ERR_UNSUPPORTED;  // the caller sizes it with attention_decode_tc_splits
+  int64_t chunk = 0;
+  const int splits = attention_decode_tc_splits(s_kv, n_kv_heads, &chunk);
+  p.ws = ws;
+  p.splits = splits;
+  p.chunk = chunk;
+  p.nst = 1;
+  {
+    const int rc = configure_decode_tc<128, kDtWs>();
+    if (rc != ENGINE_OK) return rc;
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = decode_tc_config<128, kDtWs>(p, hk, stream, attr);
+    B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtWs>, tq, tk, tv, p));
+  }
   return check_launch("attention_decode");
 }
 

@@ -73,16 +73,17 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
                          float* lse, cudaStream_t stream);
 
 /// Attention decode on tcgen05 (attention_tc.cu): one query position, d = 128,
-/// up to 16 query heads per KV head; `splits` splits of `chunk` keys (a multiple
-/// of 128) per KV head, each writing (m, l, O) to ws[n_heads][splits][d + 2]
-/// for attn_merge_kernel, or out / lse directly when splits == 1; nst = 1 or 2
-/// K / V ring stages (1: 77 KB of shared memory, two CTAs per SM).  Returns
-/// ENGINE_ERR_UNSUPPORTED, with nothing launched, for shapes or alignments it
-/// does not take.
+/// up to 16 query heads per KV head.  Up to 8 key blocks of 128 per KV head are
+/// split over one thread-block cluster and merged through distributed shared
+/// memory; longer key ranges are split over about two CTAs per SM, each
+/// writing (m, l, O) to ws[n_heads][splits][d + 2], which the caller merges with
+/// attn_merge_kernel.  attention_decode_tc_splits returns that split count (0:
+/// no workspace) and the keys per split.  Returns ENGINE_ERR_UNSUPPORTED, with
+/// nothing launched, for shapes or alignments it does not take.
+int attention_decode_tc_splits(int64_t s_kv, int64_t n_kv_heads, int64_t* chunk);
 int attention_decode_tc(const __half* q, const __half* k, const __half* v, __half* out, float* lse,
                         float* ws, int64_t s_kv, int64_t n_heads, int64_t n_kv_heads, int64_t d,
-                        int64_t kv_head_stride, float scale, int splits, int64_t chunk,
-                        int nst, cudaStream_t stream);
+                        int64_t kv_head_stride, float scale, cudaStream_t stream);
 
 /// Zeroes the stream-K tile counters of every workspace on `dev` (after a
 /// device-side time-out may have left a launch half counted).  The device must

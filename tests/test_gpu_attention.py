@@ -199,6 +199,34 @@ def test_decode_bulk_path_matches_oracle(pkg, dev, kv_len, h, h_kv, d, split):
     assert torch.equal(out, pkg.ops.attention_decode(qd, kd, vd, _scale(d), split))
 
 
+@pytest.mark.parametrize("kv_len,h,h_kv", [
+    (129, 16, 8),    # 2 query heads per KV head, 2 key blocks (cluster of 2, partial block)
+    (640, 64, 8),    # 8 per KV head, cluster of 5
+    (1024, 8, 8),    # 1 per KV head, cluster of 8
+    (1025, 32, 8),   # 9 key blocks: splits through the workspace, partial last block
+    (3000, 16, 1),   # 16 query heads on one KV head (the widest group the MMA takes)
+    (300, 32, 1)])   # 32 per KV head: beyond the tcgen05 decode, the bulk kernel
+def test_decode_tcgen05_groups_and_splits(pkg, dev, kv_len, h, h_kv):
+    """attention_decode at head_dim 128 with automatic splits runs on tcgen05:
+    GQA groups of 1-16 heads, split merges inside a cluster and through the
+    workspace; compared with the oracle (pinned to the reference's
+    attention_cpu) under the reference's tolerances, and the LSE through the
+    one-row non-causal prefill entry."""
+    rng = np.random.default_rng(kv_len * 7 + h)
+    q, k, v = _rand(rng, 1, h, h_kv, kv_len, 128)
+    want, want_lse = oracle.attention(q, k, v, _scale(128), 0, False)
+    qd, kd, vd = (torch.from_numpy(a).to(dev) for a in (q[0], k, v))
+    out = pkg.ops.attention_decode(qd, kd, vd, _scale(128))
+    (rt, at), (lrt, lat) = _tol(kv_len)
+    _close(out.cpu().numpy().astype(np.float32), want[0].astype(np.float32), rt, at,
+           f"tc decode kv_len={kv_len} h={h} h_kv={h_kv}")
+    assert torch.equal(out, pkg.ops.attention_decode(qd, kd, vd, _scale(128)))
+    out2, lse = pkg.ops.attention(qd[None], kd, vd, _scale(128), 0, False, want_lse=True)
+    _close(out2[0].cpu().numpy().astype(np.float32), want[0].astype(np.float32), rt, at,
+           "one-row prefill")
+    _close(lse.cpu().numpy(), want_lse, lrt, lat, "one-row prefill lse")
+
+
 def test_prefill_throughput_llama8b(pkg, dev):
     """Prints the tcgen05 prefill's rate at Llama-3-8B, S = 2048 causal (not asserted)."""
     H, H_kv, d, S = 32, 8, 128, 2048
