@@ -79,6 +79,9 @@ EXPORTS: dict[str, list] = {
                                       ctypes.c_int, _p, _p],
     "engine_cuda_attention_decode": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _f, ctypes.c_int,
                                      _p],
+    "engine_cuda_kv_cache_write": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
+    "engine_cuda_kv_cache_write_rows": [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _p],
     "engine_gguf_open": [ctypes.c_char_p, _P(ctypes.c_void_p)],
     "engine_gguf_close": [_p],
     "engine_gguf_version": [_p, _P(ctypes.c_int32), _P(ctypes.c_uint64)],

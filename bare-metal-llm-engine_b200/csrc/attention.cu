@@ -655,6 +655,70 @@ int run_attention(const __half* q, const __half* k, const __half* v, __half* out
   return check_launch(what);
 }
 
+// ---------------------------------------------------------------- KV cache write
+//
+// Scatters token-major K / V rows into head-major caches (the engine's
+// kv_cache_write, kernels.hpp:184; kernels/attention_bridge.cu:87), for
+// n_seq sequences of s_new tokens each: source row r = b * s_new + t holds
+// K[b, t] at k_new + r * row_pitch as [n_kv_heads][head_dim] (row_pitch = the
+// row length for the engine's contiguous form; the Q/K/V projection's output
+// row for the fused form), and lands at
+// cache[((b * n_kv_heads + h) * kv_max_seq_len + pos_offset + t) * head_dim].
+// One thread per 16 bytes when everything is 16-byte aligned, else per element;
+// a pure copy (bit-exact).
+template <bool VEC>
+__global__ void kv_cache_write_kernel(const __half* __restrict__ k_new,
+                                      const __half* __restrict__ v_new, int64_t row_pitch,
+                                      __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+                                      int64_t n_seq, int64_t s_new, int64_t n_kv_heads,
+                                      int64_t head_dim, int64_t pos_offset, int64_t max_len) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int W = VEC ? 8 : 1;  // halves per thread
+  const int64_t per_row = n_kv_heads * head_dim / W;
+  const int64_t total = n_seq * s_new * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / per_row;  // source row = b * s_new + t
+    const int64_t c = (i - r * per_row) * W;  // element within the row
+    const int64_t h = c / head_dim, e = c - h * head_dim;
+    const int64_t b = r / s_new, t = r - b * s_new;
+    const int64_t dst = ((b * n_kv_heads + h) * max_len + pos_offset + t) * head_dim + e;
+    const int64_t src = r * row_pitch + c;
+    if constexpr (VEC) {
+      *reinterpret_cast<uint4*>(k_cache + dst) = *reinterpret_cast<const uint4*>(k_new + src);
+      *reinterpret_cast<uint4*>(v_cache + dst) = *reinterpret_cast<const uint4*>(v_new + src);
+    } else {
+      k_cache[dst] = k_new[src];
+      v_cache[dst] = v_new[src];
+    }
+  }
+}
+
+int kv_cache_write_impl(const __half* k_new, const __half* v_new, int64_t row_pitch,
+                        __half* k_cache, __half* v_cache, int64_t n_seq, int64_t s_new,
+                        int64_t n_kv_heads, int64_t head_dim, int64_t pos_offset, int64_t max_len,
+                        cudaStream_t st) {
+  const bool vec = head_dim % 8 == 0 && row_pitch % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+                     reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) %
+                    16) == 0;
+  const int64_t units = n_seq * s_new * n_kv_heads * head_dim / (vec ? 8 : 1);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  const int64_t blocks = (units + 255) / 256;
+  const unsigned grid = static_cast<unsigned>(blocks < cap ? blocks : cap);
+  if (vec) {
+    B200_CUDA(launch_pdl(kv_cache_write_kernel<true>, dim3(grid), dim3(256), 0, st, k_new, v_new,
+                         row_pitch, k_cache, v_cache, n_seq, s_new, n_kv_heads, head_dim,
+                         pos_offset, max_len));
+  } else {
+    B200_CUDA(launch_pdl(kv_cache_write_kernel<false>, dim3(grid), dim3(256), 0, st, k_new, v_new,
+                         row_pitch, k_cache, v_cache, n_seq, s_new, n_kv_heads, head_dim,
+                         pos_offset, max_len));
+  }
+  return check_launch("kv_cache_write");
+}
+
 }  // namespace
 }  // namespace b200
 
@@ -731,6 +795,56 @@ int engine_cuda_attention_decode(const engine_half_t* q, const engine_half_t* k,
                        reinterpret_cast<const __half*>(v), reinterpret_cast<__half*>(out), 1,
                        kv_len, n_heads, n_kv_heads, head_dim, kv_head_stride, scale, 0, false,
                        nullptr, split_kv, static_cast<cudaStream_t>(stream), "attention_decode");
+  B200_ENTRY_END
+}
+
+int engine_cuda_kv_cache_write(const engine_half_t* k_new, const engine_half_t* v_new,
+                               engine_half_t* k_cache, engine_half_t* v_cache, int64_t s_new,
+                               int64_t n_kv_heads, int64_t head_dim, int64_t pos_offset,
+                               int64_t kv_max_seq_len, engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  // The engine's checks and messages (kernels/attention_bridge.cu:89-103).
+  B200_REQUIRE(s_new >= 0, "kv_cache_write: s_new must be non-negative");
+  B200_REQUIRE(n_kv_heads > 0, "kv_cache_write: n_kv_heads must be positive");
+  B200_REQUIRE(head_dim > 0, "kv_cache_write: head_dim must be positive");
+  B200_REQUIRE(pos_offset >= 0, "kv_cache_write: pos_offset must be non-negative");
+  B200_REQUIRE(kv_max_seq_len >= pos_offset + s_new,
+               "kv_cache_write: kv_max_seq_len < pos_offset + s_new");
+  if (s_new == 0) return ENGINE_OK;
+  B200_REQUIRE(k_new != nullptr && v_new != nullptr, "kv_cache_write: k_new/v_new is null");
+  B200_REQUIRE(k_cache != nullptr && v_cache != nullptr, "kv_cache_write: k_cache/v_cache is null");
+  return kv_cache_write_impl(reinterpret_cast<const __half*>(k_new),
+                             reinterpret_cast<const __half*>(v_new), n_kv_heads * head_dim,
+                             reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache),
+                             1, s_new, n_kv_heads, head_dim, pos_offset, kv_max_seq_len,
+                             static_cast<cudaStream_t>(stream));
+  B200_ENTRY_END
+}
+
+int engine_cuda_kv_cache_write_rows(const engine_half_t* k_new, const engine_half_t* v_new,
+                                    int64_t row_pitch, engine_half_t* k_cache,
+                                    engine_half_t* v_cache, int64_t n_seq, int64_t s_new,
+                                    int64_t n_kv_heads, int64_t head_dim, int64_t pos_offset,
+                                    int64_t kv_max_seq_len, engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(n_seq >= 0, "kv_cache_write_rows: n_seq must be non-negative");
+  B200_REQUIRE(s_new >= 0, "kv_cache_write_rows: s_new must be non-negative");
+  B200_REQUIRE(n_kv_heads > 0, "kv_cache_write_rows: n_kv_heads must be positive");
+  B200_REQUIRE(head_dim > 0, "kv_cache_write_rows: head_dim must be positive");
+  B200_REQUIRE(row_pitch >= n_kv_heads * head_dim,
+               "kv_cache_write_rows: row_pitch < n_kv_heads * head_dim");
+  B200_REQUIRE(pos_offset >= 0, "kv_cache_write_rows: pos_offset must be non-negative");
+  B200_REQUIRE(kv_max_seq_len >= pos_offset + s_new,
+               "kv_cache_write_rows: kv_max_seq_len < pos_offset + s_new");
+  if (s_new == 0 || n_seq == 0) return ENGINE_OK;
+  B200_REQUIRE(k_new != nullptr && v_new != nullptr, "kv_cache_write_rows: k_new/v_new is null");
+  B200_REQUIRE(k_cache != nullptr && v_cache != nullptr,
+               "kv_cache_write_rows: k_cache/v_cache is null");
+  return kv_cache_write_impl(reinterpret_cast<const __half*>(k_new),
+                             reinterpret_cast<const __half*>(v_new), row_pitch,
+                             reinterpret_cast<__half*>(k_cache), reinterpret_cast<__half*>(v_cache),
+                             n_seq, s_new, n_kv_heads, head_dim, pos_offset, kv_max_seq_len,
+                             static_cast<cudaStream_t>(stream));
   B200_ENTRY_END
 }
 

@@ -1020,16 +1020,28 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
 
 namespace b200 {
 
-int attention_decode_tc_splits(int64_t s_kv, int64_t n_kv_heads, int64_t* chunk) {
+// Split plan: about two CTAs per SM over all KV heads (single-stage K / V
+// rings, 79 KB of shared memory each), whole 128-key blocks per split.  One
+// split per head writes out directly; up to 8 merge inside a cluster
+// (portable size); more go through the workspace and attn_merge_kernel.
+// (Clusters of 16 were measured: a GPC rarely has 16 free SMs, so they could
+// not all be resident.)
+struct DtPlan {
+  int splits;
+  int64_t chunk;
+};
+
+DtPlan decode_tc_plan(int64_t s_kv, int64_t n_kv_heads) {
   const int64_t nblocks = (s_kv + kDtBlock - 1) / kDtBlock;
-  if (nblocks <= 8) {
-    *chunk = kDtBlock;
-    return 0;  // merged inside a cluster: no workspace
-  }
   const int64_t want = std::max<int64_t>(1, (2 * static_cast<int64_t>(sm_count())) / n_kv_heads);
   const int64_t bpc = (nblocks + want - 1) / want;  // blocks per split
-  *chunk = bpc * kDtBlock;
-  return static_cast<int>((nblocks + bpc - 1) / bpc);
+  return {static_cast<int>((nblocks + bpc - 1) / bpc), bpc * kDtBlock};
+}
+
+int attention_decode_tc_splits(int64_t s_kv, int64_t n_kv_heads, int64_t* chunk) {
+  const DtPlan pl = decode_tc_plan(s_kv, n_kv_heads);
+  *chunk = pl.chunk;
+  return pl.splits <= 8 ? 0 : pl.splits;  // 0: no workspace
 }
 
 int attention_decode_tc(const __half* q, const __half* k, const __half* v, __half* out, float* lse,
@@ -1061,43 +1073,27 @@ int attention_decode_tc(const __half* q, const __half* k, const __half* v, __hal
   p.c = scale * 1.4426950408889634f;
   p.err = device_error_word();
   p.limit_ns = wait_limit_ns();
-  // Splits of whole 128-key blocks.  Up to 8 blocks per KV head: one split per
-  // block, merged inside a cluster of at most 8 CTAs (portable size).  More:
-  // about two CTAs per SM over all heads (single-stage K / V rings, 79 KB of
-  // shared memory each), merged by attn_merge_kernel through the workspace.
-  // (Clusters of 16 cannot all be resident on B200 -- a GPC rarely has 16 free
-  // SMs -- and clusters of 8 leave half the SMs idle on long contexts.)
-  const int64_t nblocks = (s_kv + kDtBlock - 1) / kDtBlock;
+  const DtPlan pl = decode_tc_plan(s_kv, n_kv_heads);
   const unsigned hk = static_cast<unsigned>(n_kv_heads);
-  if (nblocks <= 8) {
-    p.splits = static_cast<int>(nblocks);
-    p.chunk = kDtBlock;
-    p.nst = 1;
-    cudaLaunchAttribute attr[2];
-    if (p.splits == 1) {
-      const int rc = configure_decode_tc<128, kDtFinal>();
-      if (rc != ENGINE_OK) return rc;
-      cudaLaunchConfig_t cfg = decode_tc_config<128, kDtFinal>(p, hk, stream, attr);
-      B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtFinal>, tq, tk, tv, p));
-    } else {
-      const int rc = configure_decode_tc<128, kDtCluster>();
-      if (rc != ENGINE_OK) return rc;
-      cudaLaunchConfig_t cfg = decode_tc_config<128, kDtCluster>(p, hk, stream, attr);
-      B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtCluster>, tq, tk, tv, p));
-    }
-    return check_launch("attention_decode");
-  }
-  if (ws == nullptr) return ENGINE_ERR_UNSUPPORTED;  // the caller sizes it with attention_decode_tc_splits
-  int64_t chunk = 0;
-  const int splits = attention_decode_tc_splits(s_kv, n_kv_heads, &chunk);
-  p.ws = ws;
-  p.splits = splits;
-  p.chunk = chunk;
+  p.splits = pl.splits;
+  p.chunk = pl.chunk;
   p.nst = 1;
-  {
+  cudaLaunchAttribute attr[2];
+  if (pl.splits == 1) {
+    const int rc = configure_decode_tc<128, kDtFinal>();
+    if (rc != ENGINE_OK) return rc;
+    cudaLaunchConfig_t cfg = decode_tc_config<128, kDtFinal>(p, hk, stream, attr);
+    B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtFinal>, tq, tk, tv, p));
+  } else if (pl.splits <= 8) {
+    const int rc = configure_decode_tc<128, kDtCluster>();
+    if (rc != ENGINE_OK) return rc;
+    cudaLaunchConfig_t cfg = decode_tc_config<128, kDtCluster>(p, hk, stream, attr);
+    B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtCluster>, tq, tk, tv, p));
+  } else {
+    if (ws == nullptr) return ENGINE_ERR_UNSUPPORTED;  // sized by attention_decode_tc_splits
+    p.ws = ws;
     const int rc = configure_decode_tc<128, kDtWs>();
     if (rc != ENGINE_OK) return rc;
-    cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = decode_tc_config<128, kDtWs>(p, hk, stream, attr);
     B200_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_tc_kernel<128, kDtWs>, tq, tk, tv, p));
   }

@@ -73,11 +73,11 @@ int attention_prefill_tc(const __half* q, const __half* k, const __half* v, __ha
                          float* lse, cudaStream_t stream);
 
 /// Attention decode on tcgen05 (attention_tc.cu): one query position, d = 128,
-/// up to 16 query heads per KV head.  Up to 8 key blocks of 128 per KV head are
-/// split over one thread-block cluster and merged through distributed shared
-/// memory; longer key ranges are split over about two CTAs per SM, each
-/// writing (m, l, O) to ws[n_heads][splits][d + 2], which the caller merges with
-/// attn_merge_kernel.  attention_decode_tc_splits returns that split count (0:
+/// up to 16 query heads per KV head.  The keys of each KV head are split, in
+/// whole 128-key blocks, so that all heads together give about two CTAs per SM:
+/// one split writes the output directly, up to 8 merge inside a thread-block
+/// cluster through distributed shared memory, more write (m, l, O) to
+/// ws[n_heads][splits][d + 2], which the caller merges with attn_merge_kernel.  attention_decode_tc_splits returns that split count (0:
 /// no workspace) and the keys per split.  Returns ENGINE_ERR_UNSUPPORTED, with
 /// nothing launched, for shapes or alignments it does not take.
 int attention_decode_tc_splits(int64_t s_kv, int64_t n_kv_heads, int64_t* chunk);

@@ -57,6 +57,19 @@ def attention_decode(q, k, v, out, kv_len, n_heads, n_kv_heads, head_dim,  # ker
                                               kv_head_stride, scale, split_kv, _s(stream)))
 
 
+def kv_cache_write(k_new, v_new, k_cache, v_cache, s_new, n_kv_heads, head_dim,  # kernels.hpp:184
+                   pos_offset, kv_max_seq_len, stream=0):
+    _check(lib().engine_cuda_kv_cache_write(k_new, v_new, k_cache, v_cache, s_new, n_kv_heads,
+                                            head_dim, pos_offset, kv_max_seq_len, _s(stream)))
+
+
+def kv_cache_write_rows(k_new, v_new, row_pitch, k_cache, v_cache, n_seq, s_new, n_kv_heads,
+                        head_dim, pos_offset, kv_max_seq_len, stream=0):
+    _check(lib().engine_cuda_kv_cache_write_rows(k_new, v_new, row_pitch, k_cache, v_cache, n_seq,
+                                                 s_new, n_kv_heads, head_dim, pos_offset,
+                                                 kv_max_seq_len, _s(stream)))
+
+
 def rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, stream=0):  # kernels.hpp:97
     _check(lib().engine_cuda_rmsnorm_linear(inp, rms_weight, W, out, M, N, K, eps, _s(stream)))
 

@@ -184,6 +184,56 @@ def attention_decode(q, k, v, scale=None, split_kv: int = 0):
     return out
 
 
+def kv_cache_write(k_rows, v_rows, k_cache, v_cache, pos: int, n_seq: int = 1):
+    """Scatters K / V rows into head-major caches [n_seq * H_kv, max_len, d] at
+    positions pos.. (engine::cuda::detail::kv_cache_write, batched over n_seq
+    sequences).  k_rows / v_rows are [n_seq * s_new, H_kv * d] views whose rows
+    may be strided (e.g. the K and V columns of a fused Q/K/V projection)."""
+    for t, n in ((k_rows, "k_rows"), (v_rows, "v_rows"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        if t.dtype != torch.float16 or not t.is_cuda:
+            raise TypeError(f"{n} must be a CUDA float16 tensor")
+    if k_rows.stride(1) != 1 or v_rows.stride(1) != 1 or k_rows.stride(0) != v_rows.stride(0):
+        raise ValueError("k_rows / v_rows: rows must be contiguous and share one pitch")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous [n_seq * H_kv, max_len, d]")
+    hk, max_len, d = k_cache.shape
+    H_kv = hk // n_seq
+    s_new = k_rows.shape[0] // n_seq
+    if k_rows.shape[1] != H_kv * d:
+        raise ValueError("k_rows: width != H_kv * d")
+    _c.kv_cache_write_rows(k_rows.data_ptr(), v_rows.data_ptr(), k_rows.stride(0), k_cache.data_ptr(),
+                           v_cache.data_ptr(), n_seq, s_new, H_kv, d, pos, max_len, _stream())
+
+
+def attention_cached(q, k_cache, v_cache, kv_len: int, q_pos_offset: int, is_causal: bool = True,
+                     scale=None, out=None):
+    """attention_prefill of q [s_q, H, d] over the first kv_len positions of the
+    caches [H_kv, max_len, d] (kv_head_stride = max_len * d)."""
+    _req(q, torch.float16, "q")
+    s_q, H, d = q.shape
+    H_kv, max_len, _ = k_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    o = out if out is not None else torch.empty_like(q)
+    _c.attention_prefill(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), s_q,
+                         kv_len, H, H_kv, d, max_len * d, scale, q_pos_offset, is_causal, 0,
+                         _stream())
+    return o
+
+
+def attention_decode_cached(q, k_cache, v_cache, kv_len: int, scale=None, out=None):
+    """attention_decode of one query row per head, q [H, d], over the first
+    kv_len positions of the caches [H_kv, max_len, d]; a batch of equal-length
+    sequences is q [B * H, d] over caches [B * H_kv, max_len, d]."""
+    _req(q, torch.float16, "q")
+    H, d = q.shape
+    H_kv, max_len, _ = k_cache.shape
+    scale = d ** -0.5 if scale is None else scale
+    o = out if out is not None else torch.empty_like(q)
+    _c.attention_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), kv_len,
+                        H, H_kv, d, max_len * d, scale, 0, _stream())
+    return o
+
+
 def swiglu(gate, up, out=None):
     _req(gate, torch.float16, "gate")
     _req(up, torch.float16, "up")

@@ -14,13 +14,22 @@ style over t ranks:
 * LM head [128256, 4096] vocab split; greedy sampling = local argmax, then a
   tiny all-gather of (value, index) pairs.
 
-Per layer: x -> rmsnorm_linear(QKV) -> [attention stand-in] -> linear(O) ->
-all-reduce -> rmsnorm_linear_swiglu(gate/up, SwiGLU fused) -> linear(down) ->
-all-reduce.
+Per layer: x -> rmsnorm_linear(QKV) -> attention -> linear(O) -> all-reduce ->
+rmsnorm_linear_swiglu(gate/up, SwiGLU fused) -> linear(down) -> all-reduce.
 The residual add is folded into rank 0's O / down epilogue, so the all-reduced
-sum is already x + sum_r proj_r.  Attention itself is out of scope for this
-hot path: the stand-in passes each rank's q-head slice straight to O, which
-keeps every token row independent (a row-sampled oracle stays exact).
+sum is already x + sum_r proj_r.
+
+Attention is local to a rank (its query heads and their KV heads).  With
+``enable_attention`` the layer set keeps per-layer head-major K / V caches and
+runs the library's attention: the Q/K/V projection's K and V columns are
+scattered into the caches (engine_cuda_kv_cache_write_rows), a prefill of one
+sequence runs the tcgen05 FlashAttention kernel (attention_prefill, causal,
+from the cached position), and decode -- one new token for each of n_seq
+equal-length sequences -- is ONE attention_decode call with the sequences
+folded into the KV-head dimension.  No RoPE is applied (positional encoding is
+outside this hot path).  Without it, the stand-in passes each rank's q-head
+slice straight to O, which keeps every token row independent (a row-sampled
+oracle stays exact; the CPU tests use this form).
 
 The ``ops`` object performs the projections.  ``CudaOps`` is the product path
 (the CUDA library); tests inject a CPU double to check the sharding and the
@@ -128,6 +137,15 @@ class CudaOps:
     def rmsnorm_linear_swiglu(self, x, gamma, W_gu, eps, out=None):
         return self._o.rmsnorm_linear_swiglu(x, gamma, W_gu, eps, out=out)
 
+    def kv_cache_write(self, k_rows, v_rows, k_cache, v_cache, pos, n_seq=1):
+        self._o.kv_cache_write(k_rows, v_rows, k_cache, v_cache, pos, n_seq)
+
+    def attention_prefill(self, q, k_cache, v_cache, kv_len, q_pos_offset):
+        return self._o.attention_cached(q, k_cache, v_cache, kv_len, q_pos_offset, True)
+
+    def attention_decode(self, q, k_cache, v_cache, kv_len):
+        return self._o.attention_decode_cached(q, k_cache, v_cache, kv_len)
+
     def embedding(self, table, ids, out=None):
         return self._o.embedding(table, ids, out=out)
 
@@ -222,6 +240,48 @@ class TPLayerSet:
         self.ops = ops if ops is not None else CudaOps()
         self.group = group
         self.allreduce_count = 0
+        self.kv = None  # per-layer (k_cache, v_cache) once enable_attention ran
+        self.pos = 0  # cached positions before this step (every sequence alike)
+        self.n_seq = 1
+        self.max_len = 0
+
+    def enable_attention(self, max_len: int, n_seq: int = 1, pos: int = 0):
+        """Replaces the stand-in by attention over per-layer K / V caches
+        [n_seq * n_kv_heads / t, max_len, head_dim] (zero-filled).  ``pos`` =
+        positions already cached; a step attends to positions [0, pos + new)
+        and does not advance ``pos`` (set it between steps)."""
+        cfg = self.cfg
+        hk = cfg.n_kv_heads // self.world
+        dev = self.embed.device
+        self.kv = [(torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=torch.float16),
+                    torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=torch.float16))
+                   for _ in self.layers]
+        self.n_seq, self.max_len, self.pos = n_seq, max_len, pos
+
+    def _attention(self, qkv, li: int):
+        """Rank-local attention of one layer: qkv [rows, (hq + 2 hk) * d] -> [rows, hq * d]."""
+        cfg, ops = self.cfg, self.ops
+        d = cfg.head_dim
+        hq = cfg.n_heads // self.world
+        hk = cfg.n_kv_heads // self.world
+        qd, kd = hq * d, hk * d
+        rows = qkv.shape[0]
+        kc, vc = self.kv[li]
+        q = qkv[:, :qd].contiguous()
+        k_rows, v_rows = qkv[:, qd:qd + kd], qkv[:, qd + kd:qd + 2 * kd]
+        if self.n_seq > 1 or rows == 1:  # decode: one new token per sequence
+            if rows != self.n_seq:
+                raise ValueError(f"decode step of {rows} tokens for {self.n_seq} sequences")
+            if self.pos + 1 > self.max_len:
+                raise ValueError("KV cache full")
+            ops.kv_cache_write(k_rows, v_rows, kc, vc, self.pos, n_seq=rows)
+            out = ops.attention_decode(q.view(rows * hq, d), kc, vc, self.pos + 1)
+        else:  # prefill of one sequence: `rows` tokens from position pos
+            if self.pos + rows > self.max_len:
+                raise ValueError("KV cache full")
+            ops.kv_cache_write(k_rows, v_rows, kc, vc, self.pos, n_seq=1)
+            out = ops.attention_prefill(q.view(rows, hq, d), kc, vc, self.pos + rows, self.pos)
+        return out.view(rows, qd)
 
     def _all_reduce(self, t):
         if self.world > 1:
@@ -236,9 +296,12 @@ class TPLayerSet:
         lead = self.rank == 0
         fused = (self.comm is not None and self.world > 1
                  and self.comm.fits(x.shape[0], cfg.d_model))
-        for L in self.layers:
+        for li, L in enumerate(self.layers):
             qkv = ops.rmsnorm_linear(x, L["attn_norm"], L["qkv"], cfg.eps)
-            attn = qkv[:, :qd].contiguous()  # attention stand-in (out of scope)
+            if self.kv is not None:
+                attn = self._attention(qkv, li)
+            else:
+                attn = qkv[:, :qd].contiguous()  # stand-in: the q-head slice
             x = self._row_split(attn, L["o"], x, lead, fused)
             # gate/up projection with the SwiGLU fused (one kernel at batch 1)
             h = ops.rmsnorm_linear_swiglu(x, L["ffn_norm"], L["gate_up"], cfg.eps)
@@ -332,6 +395,21 @@ def flops_per_token(cfg: TPConfig) -> float:
     return 2.0 * (cfg.n_layers * per_layer + cfg.vocab * cfg.d_model)
 
 
+# Decode steps attend to this many cached positions (the new token included).
+DECODE_CONTEXT = 1024
+
+
+def attention_prefill_flops(cfg: TPConfig, S: int) -> float:
+    """Causal attention of an S-token prefill from position 0, all layers:
+    Q K^T and P V over the S (S + 1) / 2 visible (row, key) pairs."""
+    return 4.0 * cfg.head_dim * cfg.n_heads * S * (S + 1) / 2 * cfg.n_layers
+
+
+def kv_bytes_per_rank(cfg: TPConfig, world: int, n_seq: int, kv_len: int) -> float:
+    """K and V bytes a decode step reads from the caches on one rank."""
+    return 2.0 * 2 * cfg.n_layers * n_seq * (cfg.n_kv_heads // world) * kv_len * cfg.head_dim
+
+
 # ------------------------------------------------------------------ benchmark
 
 def bench_main(args, metric: str) -> int:
@@ -355,6 +433,10 @@ def bench_main(args, metric: str) -> int:
         comm = NvlinkComm(rank, world, B * cfg.d_model)
         collective = "nvlink one-shot all-reduce fused into the O / down projection"
     model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=comm)
+    if prefill:
+        model.enable_attention(B)
+    else:
+        model.enable_attention(DECODE_CONTEXT, n_seq=B, pos=DECODE_CONTEXT - 1)
     gen = torch.Generator(device=dev).manual_seed(7)
     ids = torch.randint(0, cfg.vocab, (B,), device=dev, generator=gen, dtype=torch.int32)
     if world > 1:
@@ -398,6 +480,8 @@ def bench_main(args, metric: str) -> int:
     ms = float(t.item()) / args.steps
     tokens_s = B / (ms * 1e-3)
     wbytes = weight_bytes_per_rank(cfg, world)
+    kvb = 0.0 if prefill else kv_bytes_per_rank(cfg, world, B, DECODE_CONTEXT)
+    flops = flops_per_token(cfg) * B + (attention_prefill_flops(cfg, B) if prefill else 0.0)
     line = {
         "metric": f"Llama-3-8B-shaped TP layer set {'prefill' if prefill else 'decode'} tokens/s",
         "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -405,11 +489,14 @@ def bench_main(args, metric: str) -> int:
         "vs_baseline": None, "dtype": "f16", "data": "synthetic: random N(0,0.02) FP16 weights",
         "config": {"workload": "tp-prefill" if prefill else "tp-decode", "model": "llama3-8b-shaped",
                    "layers": cfg.n_layers, "batch": B, "parallelism": f"tp{world}",
-                   "attention": "stand-in (out of scope)", "cuda_graph": graph is not None,
+                   "attention": ("tcgen05, causal from position 0" if prefill else
+                                 f"tcgen05 decode over {DECODE_CONTEXT} cached positions"),
+                   "cuda_graph": graph is not None,
                    "collective": collective},
         "per_gpu_weight_bytes": wbytes,
-        "hbm_gbs_per_gpu": (wbytes / (ms * 1e-3) / 1e9) if not prefill else None,
-        "tflops_per_gpu": (flops_per_token(cfg) * B / world / (ms * 1e-3) / 1e12),
+        "per_gpu_kv_bytes": kvb,
+        "hbm_gbs_per_gpu": ((wbytes + kvb) / (ms * 1e-3) / 1e9) if not prefill else None,
+        "tflops_per_gpu": flops / world / (ms * 1e-3) / 1e12,
         "allreduces_per_step": 2 * cfg.n_layers if world > 1 else 0,
     }
     if rank == 0:
@@ -483,10 +570,12 @@ def tp_parity(cfg: TPConfig, world: int, rank: int, dev, comm=None) -> dict:
     m = TPLayerSet(pcfg, rank, world, shards, shard_head(lm, pcfg, world, rank), embed, fnorm)
     ops = m.ops
     B = len(TP_PARITY_TOKENS)
+    m.enable_attention(B)  # the tokens as one causal sequence: the real attention
     ref_x = torch.empty(B, pcfg.d_model, device=dev, dtype=torch.float16)
     ref_l = torch.empty(B, pcfg.vocab, device=dev, dtype=torch.float16)
     if rank == 0:
         m1 = TPLayerSet(pcfg, 0, 1, [shard_layer(L, pcfg, 1, 0) for L in layers], lm, embed, fnorm)
+        m1.enable_attention(B)
         x1 = m1.hidden(ops.embedding(embed, ids))
         ref_x.copy_(x1)
         ref_l.copy_(m1.logits_shard(x1))
@@ -604,7 +693,9 @@ def bench_tp_block(steps: int, warmup: int, hbm_peak: float, tensor_peak: float,
     cfg = LLAMA3_8B
     comm = NvlinkComm(rank, world, 32 * cfg.d_model) if world > 1 else None
     out = {"t": world, "model": "llama3-8b-shaped", "layers": cfg.n_layers,
-           "attention": "stand-in (out of scope)",
+           "attention": (f"the library's tcgen05 attention over per-layer KV caches: decode attends "
+                         f"to {DECODE_CONTEXT} cached positions (batch = sequences), prefill is "
+                         f"causal from position 0; no RoPE"),
            "nccl_ranks": dist.get_world_size() if dist.is_initialized() else 0,
            "collective_decode": ("nvlink one-shot all-reduce fused into the O / down projection"
                                  if comm is not None else "none (t = 1)"),
@@ -622,21 +713,27 @@ def bench_tp_block(steps: int, warmup: int, hbm_peak: float, tensor_peak: float,
     gen = torch.Generator(device=dev).manual_seed(7)
     for B in (1, 32):
         model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=comm)
+        model.enable_attention(DECODE_CONTEXT, n_seq=B, pos=DECODE_CONTEXT - 1)
         ids = torch.randint(0, cfg.vocab, (B,), device=dev, generator=gen, dtype=torch.int32)
         if world > 1:
             dist.broadcast(ids, 0)
         ms = _time_tp_step(model, ids, max(steps, 10), warmup, True, world, dev)
-        gbs = wbytes / (ms * 1e-3) / 1e9
+        kvb = kv_bytes_per_rank(cfg, world, B, DECODE_CONTEXT)
+        gbs = (wbytes + kvb) / (ms * 1e-3) / 1e9
         out[f"decode_b{B}"] = {"ms_per_step": ms, "tokens_s": B / (ms * 1e-3),
+                               "kv_bytes_per_gpu": kvb,
                                "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / hbm_peak}
+        del model
+        torch.cuda.empty_cache()
     # prefill S = 2048, eager (16 MiB all-reduces over NCCL)
     S = 2048
     model = TPLayerSet(cfg, rank, world, layers, lm, embed, fnorm, comm=None)
+    model.enable_attention(S)
     ids = torch.randint(0, cfg.vocab, (S,), device=dev, generator=gen, dtype=torch.int32)
     if world > 1:
         dist.broadcast(ids, 0)
     ms = _time_tp_step(model, ids, max(3, min(steps, 8)), min(warmup, 3), False, world, dev)
-    tf = flops_per_token(cfg) * S / world / (ms * 1e-3) / 1e12
+    tf = (flops_per_token(cfg) * S + attention_prefill_flops(cfg, S)) / world / (ms * 1e-3) / 1e12
     out["prefill_s2048"] = {"ms_per_step": ms, "tokens_s": S / (ms * 1e-3),
                             "tflops_per_gpu": tf, "tensor_frac_per_gpu": tf / tensor_peak}
     # The all-reduces alone at the step's message sizes (64 per step), for the share.

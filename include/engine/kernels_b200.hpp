@@ -218,6 +218,17 @@ inline void attention_decode(const __half* q, const __half* k, const __half* v, 
       b200_detail::h(q), b200_detail::h(k), b200_detail::h(v), b200_detail::h(out), kv_len,
       n_heads, n_kv_heads, head_dim, kv_head_stride, scale, split_kv, stream));
 }
+namespace detail {
+// kernels.hpp:184 -- the head-major KV-cache scatter of the attention bridge.
+inline void kv_cache_write(const __half* k_new, const __half* v_new, __half* k_cache,
+                           __half* v_cache, std::int64_t s_new, std::int64_t n_kv_heads,
+                           std::int64_t head_dim, std::int64_t pos_offset,
+                           std::int64_t kv_max_seq_len, cudaStream_t stream = 0) {
+  b200_detail::check(engine_cuda_kv_cache_write(
+      b200_detail::h(k_new), b200_detail::h(v_new), b200_detail::h(k_cache),
+      b200_detail::h(v_cache), s_new, n_kv_heads, head_dim, pos_offset, kv_max_seq_len, stream));
+}
+}  // namespace detail
 #endif  // ENGINE_B200_NO_ATTENTION
 
 // -- tensor-parallel communicator (engine_tp_*) --------------------------------

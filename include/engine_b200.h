@@ -334,6 +334,31 @@ ENGINE_B200_API int engine_cuda_attention_decode(const engine_half_t* q, const e
                                                  int64_t kv_head_stride, float scale, int split_kv,
                                                  engine_stream_t stream);
 
+/* kernels.hpp:184 (detail::kv_cache_write): token-major K / V [s_new][n_kv_heads]
+ * [head_dim] scattered into head-major caches [n_kv_heads][kv_max_seq_len]
+ * [head_dim] from position pos_offset.  Same checks and messages as
+ * kernels/attention_bridge.cu:89-103.  A copy: bit-exact. */
+ENGINE_B200_API int engine_cuda_kv_cache_write(const engine_half_t* k_new, const engine_half_t* v_new,
+                                               engine_half_t* k_cache, engine_half_t* v_cache,
+                                               int64_t s_new, int64_t n_kv_heads, int64_t head_dim,
+                                               int64_t pos_offset, int64_t kv_max_seq_len,
+                                               engine_stream_t stream);
+
+/* The same for n_seq sequences of s_new tokens read from strided rows: row
+ * b * s_new + t starts at k_new + (b * s_new + t) * row_pitch (elements), so
+ * the K and V parts of a fused Q/K/V projection's output go to the caches
+ * without a copy.  Sequence b's caches are the heads [b * n_kv_heads, (b + 1) *
+ * n_kv_heads) of k_cache / v_cache, so a batch of equal-length sequences is one
+ * attention_decode call with n_seq * n_kv_heads KV heads.  No counterpart in the
+ * reference (its kv_cache_write is the n_seq = 1, contiguous case above). */
+ENGINE_B200_API int engine_cuda_kv_cache_write_rows(const engine_half_t* k_new,
+                                                    const engine_half_t* v_new, int64_t row_pitch,
+                                                    engine_half_t* k_cache, engine_half_t* v_cache,
+                                                    int64_t n_seq, int64_t s_new,
+                                                    int64_t n_kv_heads, int64_t head_dim,
+                                                    int64_t pos_offset, int64_t kv_max_seq_len,
+                                                    engine_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * GGUF model files, memory-mapped, feeding the projections.  The engine plans a
  * GGUF-style mmap'd loader (README.md:247, Module 7; tensor.hpp:19-23: weight

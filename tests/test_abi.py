@@ -247,6 +247,24 @@ def test_quant_entries_reject_bad_arguments(pkg):
     c.quant_repack(4, P, P, P, 0, 32)      # no rows: no-op
 
 
+def test_kv_cache_write_entries_reject_bad_arguments(pkg):
+    """engine_cuda_kv_cache_write keeps the engine's checks and messages
+    (kernels/attention_bridge.cu:89-103); the strided batched form adds its own."""
+    c = pkg.cuda
+    _throws(pkg, c.kv_cache_write, P, P, P, P, -1, 8, 128, 0, 16, substr="s_new must be non-negative")
+    _throws(pkg, c.kv_cache_write, P, P, P, P, 4, 0, 128, 0, 16, substr="n_kv_heads must be positive")
+    _throws(pkg, c.kv_cache_write, P, P, P, P, 4, 8, 0, 0, 16, substr="head_dim must be positive")
+    _throws(pkg, c.kv_cache_write, P, P, P, P, 4, 8, 128, -1, 16, substr="pos_offset")
+    _throws(pkg, c.kv_cache_write, P, P, P, P, 4, 8, 128, 14, 16, substr="kv_max_seq_len <")
+    _throws(pkg, c.kv_cache_write, 0, P, P, P, 4, 8, 128, 0, 16, substr="k_new/v_new is null")
+    _throws(pkg, c.kv_cache_write, P, P, P, 0, 4, 8, 128, 0, 16, substr="k_cache/v_cache is null")
+    c.kv_cache_write(0, 0, 0, 0, 0, 8, 128, 3, 3)  # s_new == 0: no-op, null pointers allowed
+    _throws(pkg, c.kv_cache_write_rows, P, P, 100, P, P, 1, 1, 1, 128, 0, 4, substr="row_pitch")
+    _throws(pkg, c.kv_cache_write_rows, P, P, 128, P, P, -1, 1, 1, 128, 0, 4, substr="n_seq")
+    _throws(pkg, c.kv_cache_write_rows, P, P, 128, P, P, 2, 3, 1, 128, 2, 4, substr="kv_max_seq_len <")
+    c.kv_cache_write_rows(0, 0, 128, 0, 0, 0, 3, 1, 128, 0, 4)  # no sequences: no-op
+
+
 def test_c_abi_links_and_runs_from_plain_c(pkg, tmp_path):
     """include/engine_b200.h is C99 (pedantic, warnings as errors), and a plain C
     program links libengine_b200.so and makes calls that need no GPU: the ABI

@@ -227,6 +227,65 @@ def test_decode_tcgen05_groups_and_splits(pkg, dev, kv_len, h, h_kv):
     _close(lse.cpu().numpy(), want_lse, lrt, lat, "one-row prefill lse")
 
 
+@pytest.mark.parametrize("n_seq,s_new,h_kv,d,pitch_extra,pos", [
+    (1, 5, 8, 128, 0, 3),      # the engine's contiguous form (16-byte copies)
+    (3, 1, 2, 128, 4608, 7),   # three sequences, rows strided like a Q/K/V projection
+    (2, 4, 3, 6, 2, 0)])       # head_dim 6: the element-wise path
+def test_kv_cache_write_scatter_is_exact(pkg, dev, n_seq, s_new, h_kv, d, pitch_extra, pos):
+    """kv_cache_write (kernels.hpp:184) and its strided batched form against the
+    layout rule of kernels/attention_bridge.cu:45-56: token-major rows to
+    head-major caches from pos, every other position untouched, bit for bit."""
+    rng = np.random.default_rng(n_seq * 100 + s_new)
+    max_len = pos + s_new + 2
+    pitch = h_kv * d + pitch_extra
+    rows = n_seq * s_new
+    src = rng.standard_normal((rows, 2 * pitch)).astype(np.float16)
+    k_rows, v_rows = src[:, :h_kv * d], src[:, pitch:pitch + h_kv * d]
+    kc0 = rng.standard_normal((n_seq * h_kv, max_len, d)).astype(np.float16)
+    vc0 = rng.standard_normal((n_seq * h_kv, max_len, d)).astype(np.float16)
+    kc, vc = torch.from_numpy(kc0).to(dev), torch.from_numpy(vc0).to(dev)
+    ts = torch.from_numpy(src).to(dev)
+    if n_seq == 1 and pitch_extra == 0:
+        kn = torch.from_numpy(np.ascontiguousarray(k_rows)).to(dev)
+        vn = torch.from_numpy(np.ascontiguousarray(v_rows)).to(dev)
+        pkg.cuda.kv_cache_write(kn.data_ptr(), vn.data_ptr(), kc.data_ptr(), vc.data_ptr(), s_new,
+                                h_kv, d, pos, max_len)
+    else:
+        pkg.ops.kv_cache_write(ts[:, :h_kv * d], ts[:, pitch:pitch + h_kv * d], kc, vc, pos, n_seq)
+    torch.cuda.synchronize()
+    want_k, want_v = kc0.copy(), vc0.copy()
+    for b in range(n_seq):
+        for t in range(s_new):
+            r = b * s_new + t
+            want_k[b * h_kv:(b + 1) * h_kv, pos + t] = k_rows[r].reshape(h_kv, d)
+            want_v[b * h_kv:(b + 1) * h_kv, pos + t] = v_rows[r].reshape(h_kv, d)
+    assert np.array_equal(kc.cpu().numpy().view(np.uint16), want_k.view(np.uint16))
+    assert np.array_equal(vc.cpu().numpy().view(np.uint16), want_v.view(np.uint16))
+
+
+def test_batched_decode_equals_per_sequence_decode(pkg, dev):
+    """A batch of equal-length sequences as one attention_decode call (the
+    sequences folded into the KV-head dimension, as the layer set does) equals
+    one call per sequence, bit for bit, and the oracle within tolerance."""
+    rng = np.random.default_rng(41)
+    B, H, Hk, d, kv, max_len = 3, 8, 2, 128, 700, 800
+    q = rng.standard_normal((B * H, d)).astype(np.float16)
+    kc = rng.standard_normal((B * Hk, max_len, d)).astype(np.float16)
+    vc = rng.standard_normal((B * Hk, max_len, d)).astype(np.float16)
+    tq, tk, tv = (torch.from_numpy(a).to(dev) for a in (q, kc, vc))
+    batched = pkg.ops.attention_decode_cached(tq, tk, tv, kv)
+    (rt, at), _ = _tol(kv)
+    for b in range(B):
+        one = pkg.ops.attention_decode_cached(tq[b * H:(b + 1) * H].contiguous(),
+                                              tk[b * Hk:(b + 1) * Hk].contiguous(),
+                                              tv[b * Hk:(b + 1) * Hk].contiguous(), kv)
+        assert torch.equal(batched[b * H:(b + 1) * H], one), f"sequence {b}"
+        want, _ = oracle.attention(q[None, b * H:(b + 1) * H], np.ascontiguousarray(kc[b * Hk:(b + 1) * Hk, :kv]),
+                                   np.ascontiguousarray(vc[b * Hk:(b + 1) * Hk, :kv]), _scale(d), 0, False)
+        _close(one.cpu().numpy().astype(np.float32), want[0].astype(np.float32), rt, at,
+               f"decode sequence {b}")
+
+
 def test_prefill_throughput_llama8b(pkg, dev):
     """Prints the tcgen05 prefill's rate at Llama-3-8B, S = 2048 causal (not asserted)."""
     H, H_kv, d, S = 32, 8, 128, 2048

@@ -4,9 +4,11 @@
   composition of the reference's ops (rmsnorm_linear -> linear + residual ->
   rmsnorm_linear -> swiglu -> linear + residual, tests/test_kernels.cu:2813-2938)
   with FP16 rounding at the same op boundaries;
+* t = 1 with the library's attention over KV caches (prefill and a decode
+  step) against the oracle composition with the reference's attention;
 * t = 2, 4, 8 (one process per GPU; skipped when the box has fewer GPUs):
   every rank's hidden state and its logits shard against t = 1 on the same full
-  weights, sharded by the product's own shard_layer / shard_head -- once with
+  weights (the tokens as one causal sequence through the real attention), sharded by the product's own shard_layer / shard_head -- once with
   NCCL all-reduces and once with the library's NVLink communicator (the O /
   down projections fused with their all-reduce);
 * the communicator's fused call alone on t ranks: Y = sum_r X_r W_r^T + R
@@ -119,6 +121,78 @@ def test_tp_layer_set_t1_matches_oracle_composition(pkg, dev):
     assert (nxt.cpu().numpy() == lg.argmax(axis=1)).all()
 
 
+def oracle_layer_attn(x, L, cfg, k_prev=None, v_prev=None):
+    """oracle_layer with the real attention: the rows of x are the new tokens of
+    one sequence at positions P.. (P = cached positions, whose K / V rows are
+    k_prev / v_prev [H_kv, P, d]); causal attention over all positions, FP16 at
+    the op boundaries.  Returns (x_out, k_all, v_all)."""
+    f = cfg.ffn
+    d, H, Hk = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+    h = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    Wgu = np.concatenate([h(L["gate"]), h(L["up"])])
+    S = x.shape[0]
+    qkv = oracle.rmsnorm_linear_f16(x, h(L["attn_norm"]), h(L["qkv"]), cfg.eps, nthreads=8)
+    q = np.ascontiguousarray(qkv[:, :H * d].reshape(S, H, d))
+    k = qkv[:, H * d:(H + Hk) * d].reshape(S, Hk, d).transpose(1, 0, 2)
+    v = qkv[:, (H + Hk) * d:].reshape(S, Hk, d).transpose(1, 0, 2)
+    P = 0 if k_prev is None else k_prev.shape[1]
+    if P:
+        k = np.concatenate([k_prev, k], axis=1)
+        v = np.concatenate([v_prev, v], axis=1)
+    k, v = np.ascontiguousarray(k), np.ascontiguousarray(v)
+    att, _ = oracle.attention(q, k, v, d ** -0.5, P, True)
+    attn = np.ascontiguousarray(att.astype(np.float16).reshape(S, H * d))
+    x1 = oracle.linear_f16(attn, h(L["o"]), residual=x, nthreads=8)
+    gu = oracle.rmsnorm_linear_f16(x1, h(L["ffn_norm"]), Wgu, cfg.eps, nthreads=8)
+    sw = oracle.swiglu_f16(np.ascontiguousarray(gu[:, :f]), np.ascontiguousarray(gu[:, f:]))
+    return oracle.linear_f16(sw, h(L["down"]), residual=x1, nthreads=8), k, v
+
+
+def test_tp_layer_set_t1_attention_matches_oracle_composition(pkg, dev):
+    """The layer set with the library's attention over KV caches at t = 1: a
+    32-token causal prefill (the tcgen05 FlashAttention kernel) and then one
+    decode step attending to all 33 positions (the tcgen05 decode kernel),
+    each layer fed the GPU's own input and its own cache, against the oracle
+    composition with the reference's two-pass attention at the same FP16
+    boundaries."""
+    tp = pkg.tp
+    cfg = small_cfg(tp)
+    layers, lm, embed, fnorm = full_weights(cfg, dev, seed=23)
+    S = 32
+    ids = torch.randint(0, cfg.vocab, (S + 1,), device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(5), dtype=torch.int32)
+    one_cfg = dataclasses.replace(cfg, n_layers=1)
+    ones = []
+    x = pkg.ops.embedding(embed, ids[:S])
+    for li, L in enumerate(layers):
+        one = tp.TPLayerSet(one_cfg, 0, 1, [tp.shard_layer(L, cfg, 1, 0)], lm, embed, fnorm)
+        one.enable_attention(S + 1)
+        x_in = x.detach().cpu().numpy()
+        x = one.hidden(x)
+        torch.cuda.synchronize()
+        want, _, _ = oracle_layer_attn(x_in, L, cfg)
+        np.testing.assert_allclose(x.float().cpu().numpy(), want.astype(np.float32), rtol=RTOL,
+                                   atol=ATOL, err_msg=f"prefill layer {li}")
+        ones.append(one)
+    xd = pkg.ops.embedding(embed, ids[S:])
+    for li, (L, one) in enumerate(zip(layers, ones)):
+        one.pos = S
+        kc, vc = one.kv[0]
+        k_prev = kc[:, :S].cpu().numpy()
+        v_prev = vc[:, :S].cpu().numpy()
+        x_in = xd.detach().cpu().numpy()
+        xd = one.hidden(xd)
+        torch.cuda.synchronize()
+        want, k_all, v_all = oracle_layer_attn(x_in, L, cfg, k_prev, v_prev)
+        np.testing.assert_allclose(xd.float().cpu().numpy(), want.astype(np.float32), rtol=RTOL,
+                                   atol=ATOL, err_msg=f"decode layer {li}")
+        # the new token's K / V landed at position S (the GPU's projection against
+        # the oracle's: within the projection's rounding)
+        for got_c, want_c in ((kc, k_all), (vc, v_all)):
+            np.testing.assert_allclose(got_c[:, S].float().cpu().numpy(),
+                                       want_c[:, S].astype(np.float32), rtol=RTOL, atol=ATOL)
+
+
 # ------------------------------------------------------------------ t > 1
 
 def _worker(rank, world, port, q, use_comm):
@@ -141,6 +215,7 @@ def _worker(rank, world, port, q, use_comm):
         comm = tp.NvlinkComm(rank, world, len(TOKENS) * cfg.d_model) if use_comm else None
         m = build(tp, cfg, world, rank, weights)
         m.comm = comm
+        m.enable_attention(len(TOKENS))  # the tokens as one causal sequence
         x = m.hidden(pkg.ops.embedding(weights[2], ids))
         logits = m.logits_shard(x)
         nxt = m.greedy(logits)
@@ -150,6 +225,7 @@ def _worker(rank, world, port, q, use_comm):
             comm.close()
         if rank == 0:
             m1 = build(tp, cfg, 1, 0, weights)
+            m1.enable_attention(len(TOKENS))
             x1 = m1.hidden(pkg.ops.embedding(weights[2], ids))
             res["x1"] = x1.float().cpu().numpy()
             res["logits1"] = m1.logits_shard(x1).float().cpu().numpy()
