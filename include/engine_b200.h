@@ -30,8 +30,10 @@
  *   - from a library-owned stream-ordered memory pool (cached between calls):
  *     engine_cuda_rmsnorm_linear_f16 with M > 4 (normalised activation rows),
  *     engine_cuda_rmsnorm_linear_swiglu_f16 with M > 1 (the gate/up rows) and
- *     engine_cuda_attention_decode / _prefill with more than one KV split (the
- *     split partials);
+ *     engine_cuda_attention_decode / _prefill with split partials to merge (the
+ *     tcgen05 decode with more than 8 splits per KV head, or the CUDA-core
+ *     kernels with more than one; up to 8 tcgen05 splits merge inside a
+ *     thread-block cluster and need none);
  *   - once per (device, stream), on the first call that needs it, never during
  *     a stream capture: the stream-K workspace of the large 16-bit GEMMs
  *     (engine_cuda_matmul_* / linear_* with M, N >= 256; about 38 MB);
