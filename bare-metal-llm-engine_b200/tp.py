@@ -245,16 +245,18 @@ class TPLayerSet:
         self.n_seq = 1
         self.max_len = 0
 
-    def enable_attention(self, max_len: int, n_seq: int = 1, pos: int = 0):
+    def enable_attention(self, max_len: int, n_seq: int = 1, pos: int = 0,
+                         dtype=torch.float16):
         """Replaces the stand-in by attention over per-layer K / V caches
-        [n_seq * n_kv_heads / t, max_len, head_dim] (zero-filled).  ``pos`` =
-        positions already cached; a step attends to positions [0, pos + new)
-        and does not advance ``pos`` (set it between steps)."""
+        [n_seq * n_kv_heads / t, max_len, head_dim] (zero-filled; FP16 for the
+        library, float64 for the CPU test double).  ``pos`` = positions already
+        cached; a step attends to positions [0, pos + new) and does not advance
+        ``pos`` (set it between steps)."""
         cfg = self.cfg
         hk = cfg.n_kv_heads // self.world
         dev = self.embed.device
-        self.kv = [(torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=torch.float16),
-                    torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=torch.float16))
+        self.kv = [(torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=dtype),
+                    torch.zeros(n_seq * hk, max_len, cfg.head_dim, device=dev, dtype=dtype))
                    for _ in self.layers]
         self.n_seq, self.max_len, self.pos = n_seq, max_len, pos
 

@@ -51,7 +51,22 @@ def run_model(tp, cfg, world, rank, ops, group=None):
     return x, nxt, m.allreduce_count
 
 
-def _worker(rank, world, port, q, cfg_kw=None):
+def run_model_attention(tp, cfg, world, rank, ops, group=None):
+    """Prefill of four tokens (one causal sequence) and one decode step over the
+    caches, with the real per-rank attention heads."""
+    layers, lm, embed, fnorm = full_weights(cfg)
+    shards = [tp.shard_layer(L, cfg, world, rank) for L in layers]
+    m = tp.TPLayerSet(cfg, rank, world, shards, tp.shard_head(lm, cfg, world, rank), embed, fnorm,
+                      ops=ops, group=group)
+    ids = torch.tensor([0, 5, 199, 42], dtype=torch.int32)
+    m.enable_attention(5, dtype=torch.float64)
+    x = m.hidden(ops.embedding(embed, ids))
+    m.pos = 4
+    xd = m.hidden(ops.embedding(embed, torch.tensor([7], dtype=torch.int32)))
+    return torch.cat([x, xd]), m.greedy(m.logits_shard(xd)), m.allreduce_count
+
+
+def _worker(rank, world, port, q, cfg_kw=None, attention=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -63,7 +78,8 @@ def _worker(rank, world, port, q, cfg_kw=None):
 
         tp = pkg.tp
         cfg = tp.TPConfig(**(cfg_kw or CFG_KW))
-        x, nxt, n_ar = run_model(tp, cfg, world, rank, CpuOps())
+        run = run_model_attention if attention else run_model
+        x, nxt, n_ar = run(tp, cfg, world, rank, CpuOps())
         q.put((rank, x.numpy(), nxt.numpy(), n_ar))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e), None, None))
@@ -107,6 +123,39 @@ def test_tp_layer_set_matches_unsharded_on_gloo(world, cfg_kw):
         torch.testing.assert_close(torch.from_numpy(x), x1, rtol=1e-12, atol=1e-12)
         assert (nxt == n1.numpy()).all()
         assert n_ar == 2 * cfg.n_layers
+
+
+# 16 query heads on 8 KV heads: t = 8 leaves one KV head (and two query heads) per rank
+WIDE_KW = dict(CFG_KW, n_heads=16, n_kv_heads=8, d_model=128)
+
+
+@pytest.mark.parametrize("world,cfg_kw", [(2, CFG_KW), (4, CFG_KW), (8, WIDE_KW)])
+def test_tp_layer_set_with_attention_matches_unsharded_on_gloo(world, cfg_kw):
+    """The per-rank attention heads and KV caches: a causal prefill and a decode
+    step at t = 2, 4, 8 equal the unsharded run (each rank attends with its own
+    query heads over its own KV heads; two all-reduces per layer per step)."""
+    pkg = load_package()
+    from tests.tp_cpu_ops import CpuOps
+
+    tp = pkg.tp
+    cfg = tp.TPConfig(**cfg_kw)
+    x1, n1, _ = run_model_attention(tp, cfg, 1, 0, CpuOps())
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, cfg_kw, True))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=180) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, x, nxt, n_ar in results:
+        assert not isinstance(x, str), f"rank {rank} failed: {x}"
+        torch.testing.assert_close(torch.from_numpy(x), x1, rtol=1e-12, atol=1e-12)
+        assert (nxt == n1.numpy()).all()
+        assert n_ar == 4 * cfg.n_layers
 
 
 def test_qkv_shards_are_head_aligned_and_partition_the_rows():
