@@ -895,7 +895,7 @@ KERNEL_CASES = ("gemm4096", "gemv_4096x14336", "rmsnorm_qkv_b1", "rmsnorm_qkv_b1
                 "matmul_f32_512", "matmul_f32_4096", "prefill_s2048", "gate_up_swiglu_b1",
                 "tp_down_b1_world1", "tp_allreduce_b32_world1", "gemv_q8_0_4096x14336",
                 "gemv_q4_0_4096x14336", "gemv_fp16_kn_4096", "attn_prefill_s2048",
-                "attn_decode_4096")
+                "attn_decode_4096", "attn_decode_1000", "kv_cache_write_b32")
 
 
 def run_kernel_case(args) -> int:
@@ -980,6 +980,23 @@ def run_kernel_case(args) -> int:
         fn = lambda s: pkg.cuda.attention_prefill(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
                                                   s[3].data_ptr(), S, S, H, Hk, d, S * d, d ** -0.5,
                                                   0, True, 0, st)
+    elif c == "attn_decode_1000":  # 1000 keys: the splits merge inside a thread-block cluster
+        kv, H, Hk, d = 1000, 32, 8, 128
+        sets = [(torch.randn(H, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.randn(Hk, kv, d, device=dev, generator=g).half(),
+                 torch.empty(H, d, device=dev, dtype=torch.float16)) for _ in range(16)]
+        fn = lambda s: pkg.cuda.attention_decode(s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                                                 s[3].data_ptr(), kv, H, Hk, d, kv * d, d ** -0.5, 0,
+                                                 st)
+    elif c == "kv_cache_write_b32":  # decode of 32 sequences: K / V of a Q/K/V output into the caches
+        B, Hk, d, L, qkv_cols = 32, 8, 128, 1024, 6144
+        sets = [(torch.randn(B, qkv_cols, device=dev, generator=g).half(),
+                 torch.zeros(B * Hk, L, d, device=dev, dtype=torch.float16),
+                 torch.zeros(B * Hk, L, d, device=dev, dtype=torch.float16)) for _ in range(2)]
+        fn = lambda s: pkg.cuda.kv_cache_write_rows(  # noqa: E731
+            s[0].data_ptr() + 2 * 4096, s[0].data_ptr() + 2 * 5120, qkv_cols, s[1].data_ptr(),
+            s[2].data_ptr(), B, 1, Hk, d, L - 1, L, st)
     elif c == "attn_decode_4096":  # one token over 4096 keys, Llama-3-8B heads
         kv, H, Hk, d = 4096, 32, 8, 128
         sets = [(torch.randn(H, d, device=dev, generator=g).half(),
