@@ -397,7 +397,7 @@ __device__ __forceinline__ void epilogue_tma_tile(const CUtensorMap* tmC, uint8_
 }
 
 template <int BN, bool B_MN, bool SWAP, bool HILO, bool RESID, bool BF16>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, SWAP ? 2 : 1)  // SWAP: two CTAs per SM
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
@@ -586,13 +586,27 @@ __global__ void __launch_bounds__(kThreads)
 
       if (p.split > 1) {
         // Park the FP32 partial in shared memory (the pipeline ring is idle now).
+        // Each chunk's loads from all the accumulators go out before one wait,
+        // and are added in accumulator order (as ld16 does).
         float* P = reinterpret_cast<float*>(smem);
+        constexpr int CW = 16;  // 4 x 16 registers in flight: two CTAs per SM still fit
+        const int na = SWAP ? nacc : 1;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float f[16];
-          ld16(c, f);
+        for (int c = 0; c < BN; c += CW) {
+          uint32_t v[4][CW];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) P[rl * Cfg::kPartialPitch + c + i] = have_k ? f[i] : 0.0f;
+          for (int j = 0; j < 4; ++j) {
+            if (j < na) tmem_ld_32x32b_x16(taddr + j * BN + c, v[j]);
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < CW; ++i) {
+            float f = __uint_as_float(v[0][i]);
+#pragma unroll
+            for (int j = 1; j < 4; ++j)
+              if (j < na) f += __uint_as_float(v[j][i]);
+            P[rl * Cfg::kPartialPitch + c + i] = have_k ? f : 0.0f;
+          }
         }
       } else if constexpr (SWAP) {
         if constexpr (HILO) {
@@ -694,16 +708,51 @@ __global__ void __launch_bounds__(kThreads)
     const int S = p.split;
     const int my_rows = (kBM - z + S - 1) / S;
     const int cols = HILO ? p.half_b : BN;
-    for (int e = threadIdx.x; e < my_rows * cols; e += kThreads) {
-      const int r = z + S * (e / cols);
-      const int j = e % cols;
-      float v = 0.0f;
-      for (int qr = 0; qr < S; ++qr) {
-        const float* peer = cluster.map_shared_rank(P, qr);
-        v += peer[r * Cfg::kPartialPitch + j];
-        if constexpr (HILO) v += peer[r * Cfg::kPartialPitch + j + p.half_b];
+    if (cols % 4 == 0 && (!HILO || p.half_b % 4 == 0)) {
+      // Four adjacent columns per thread: one 16-byte DSMEM load per rank (two
+      // with HILO), all ranks' loads issued before the sums, which keep the
+      // rank order (hi then lo per rank) of the scalar form below.
+      const int c4 = cols / 4;
+      for (int e = threadIdx.x; e < my_rows * c4; e += kThreads) {
+        const int r = z + S * (e / c4);
+        const int j = (e % c4) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q0 = 0; q0 < 8; q0 += 4) {  // four ranks' loads in flight at a time
+          float4 a[4], b[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (q0 + i < S) {
+              const float* peer = cluster.map_shared_rank(P, q0 + i) + r * Cfg::kPartialPitch + j;
+              a[i] = *reinterpret_cast<const float4*>(peer);
+              if constexpr (HILO) b[i] = *reinterpret_cast<const float4*>(peer + p.half_b);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (q0 + i < S) {
+              v.x += a[i].x; v.y += a[i].y; v.z += a[i].z; v.w += a[i].w;
+              if constexpr (HILO) { v.x += b[i].x; v.y += b[i].y; v.z += b[i].z; v.w += b[i].w; }
+            }
+          }
+        }
+        emit<SWAP, RESID, BF16>(p, tm, tn, r, j, BN, v.x);
+        emit<SWAP, RESID, BF16>(p, tm, tn, r, j + 1, BN, v.y);
+        emit<SWAP, RESID, BF16>(p, tm, tn, r, j + 2, BN, v.z);
+        emit<SWAP, RESID, BF16>(p, tm, tn, r, j + 3, BN, v.w);
       }
-      emit<SWAP, RESID, BF16>(p, tm, tn, r, j, BN, v);
+    } else {
+      for (int e = threadIdx.x; e < my_rows * cols; e += kThreads) {
+        const int r = z + S * (e / cols);
+        const int j = e % cols;
+        float v = 0.0f;
+        for (int qr = 0; qr < S; ++qr) {
+          const float* peer = cluster.map_shared_rank(P, qr);
+          v += peer[r * Cfg::kPartialPitch + j];
+          if constexpr (HILO) v += peer[r * Cfg::kPartialPitch + j + p.half_b];
+        }
+        emit<SWAP, RESID, BF16>(p, tm, tn, r, j, BN, v);
+      }
     }
     cluster.sync();
   }
