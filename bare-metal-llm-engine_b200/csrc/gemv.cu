@@ -322,12 +322,21 @@ int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const
     }
   }
   // Persistent grid: as many CTAs as are resident at once (the prologue runs
-  // once per CTA), never more than there are row blocks.
+  // once per CTA), never more than there are row blocks.  When every CTA gets
+  // only a few row blocks, the grid shrinks so that all get the same number:
+  // a CTA with one block more than the others is the launch's tail (W[6144,4096]:
+  // 768 blocks as 256 CTAs x 3 instead of 296 CTAs with 2 or 3, 11.7 -> 11.2 us;
+  // W[4096,4096]: 8.5 -> 8.1 us; at 50+ blocks per CTA it does not pay).
   int per_sm = 0;
   B200_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNkVecWarps * 32, smem));
   if (per_sm < 1) per_sm = 1;
   const int64_t resident = static_cast<int64_t>(per_sm) * sm_count();
-  const unsigned grid = static_cast<unsigned>(nblocks < resident ? nblocks : resident);
+  int64_t g = nblocks < resident ? nblocks : resident;
+  if (g > 0) {
+    const int64_t per = (nblocks + g - 1) / g;
+    if (per <= 4) g = (nblocks + per - 1) / per;
+  }
+  const unsigned grid = static_cast<unsigned>(g);
   B200_CUDA(launch_pdl(kern, dim3(grid), dim3(kNkVecWarps * 32), smem, stream, W, X, gamma, R, Y,
                        N, K, eps));
   return ENGINE_OK;
