@@ -16,6 +16,8 @@
 // GEMV: y[n] = sum_b d[n,b] * (sum_{i<32} q[n,32b+i] * x[32b+i]) (+ residual).
 // - Each lane owns whole blocks; the 32 lanes of a warp cover 32 consecutive
 //   blocks of a row: 1 KB of Q8_0 or 512 B of Q4_0 payload per warp step.
+//   A warp group (one warp, or two splitting K) owns four rows, so each x chunk
+//   it loads from L1 is multiplied into four rows' payload.
 // - Payload loads are 16-byte `ld.global.nc.L1::no_allocate`; scales (64 B per
 //   warp step) and x come through L1.
 // - Weights are widened to exact FP16 values by bit arithmetic (no int->float
@@ -153,8 +155,9 @@ __global__ void __launch_bounds__(kQWarps * 32, 2) gemv_q_kernel(
   for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
   // Software pipeline: U blocks per lane per buffer, two buffers -- the next U
   // blocks' payload and scales are in flight while the current U are multiplied
-  // (about 256 payload bytes per lane in flight, as in the FP16 decode GEMV).
-  constexpr int U = QT == 8 ? 2 : 4;
+  // (U x RPW x 16 bytes per buffer: 128 payload bytes per lane in flight with
+  // four rows a warp).  Each x chunk loaded from L1 feeds all RPW rows.
+  constexpr int U = QT == 8 ? 1 : 2;
   constexpr int NP = QT == 8 ? 2 : 1;  // 16-byte payload words per block
   uint4 pa[U][RPW][NP], pb[U][RPW][NP];
   float sa[U][RPW], sb[U][RPW];
@@ -223,24 +226,26 @@ __global__ void __launch_bounds__(kQWarps * 32, 2) gemv_q_kernel(
   }
 }
 
+template <int QT, bool RESID, int SK>
+int launch_q_split(const uint8_t* q, const __half* d, const __half* x, const __half* R,
+                    __half* y, int64_t N, int64_t K, cudaStream_t stream) {
+  constexpr int RPW = 4;
+  constexpr int64_t rows_per_cta = (kQWarps / SK) * RPW;
+  const unsigned grid = static_cast<unsigned>((N + rows_per_cta - 1) / rows_per_cta);
+  B200_CUDA(launch_pdl(gemv_q_kernel<QT, RPW, SK, RESID>, dim3(grid), dim3(kQWarps * 32), 0,
+                       stream, q, d, x, R, y, N, K));
+  return ENGINE_OK;
+}
+
 template <int QT, bool RESID>
 int launch_gemv_q(const uint8_t* q, const __half* d, const __half* x, const __half* R, __half* y,
                   int64_t N, int64_t K, cudaStream_t stream) {
-  // Two rows per warp group; K is split over two warps when a row has few blocks.
-  constexpr int RPW = 2;
-  const int64_t nblk = K / 32;
-  if (nblk <= 256) {
-    constexpr int SK = 2;
-    const unsigned grid = static_cast<unsigned>((N + (kQWarps / SK) * RPW - 1) / ((kQWarps / SK) * RPW));
-    B200_CUDA(launch_pdl(gemv_q_kernel<QT, RPW, SK, RESID>, dim3(grid), dim3(kQWarps * 32), 0,
-                         stream, q, d, x, R, y, N, K));
-  } else {
-    constexpr int SK = 1;
-    const unsigned grid = static_cast<unsigned>((N + (kQWarps / SK) * RPW - 1) / ((kQWarps / SK) * RPW));
-    B200_CUDA(launch_pdl(gemv_q_kernel<QT, RPW, SK, RESID>, dim3(grid), dim3(kQWarps * 32), 0,
-                         stream, q, d, x, R, y, N, K));
-  }
-  return ENGINE_OK;
+  // Four rows per warp group (measured on B200 against two: 14336x4096 Q8_0
+  // 19.6 -> 15.5 us, Q4_0 17.8 -> 14.3 us; 4096x4096 7.1 -> 5.7 / 6.5 -> 4.9 us;
+  // 4096x14336 unchanged).  K is split over two warps up to 1024 blocks a row
+  // (32768 weights), so that 4096 rows still give enough warps.
+  if (K / 32 <= 1024) return launch_q_split<QT, RESID, 2>(q, d, x, R, y, N, K, stream);
+  return launch_q_split<QT, RESID, 1>(q, d, x, R, y, N, K, stream);
 }
 
 }  // namespace
