@@ -203,7 +203,10 @@ def test_decode_bulk_path_matches_oracle(pkg, dev, kv_len, h, h_kv, d, split):
     (129, 16, 8),    # 2 query heads per KV head, 2 key blocks (cluster of 2, partial block)
     (640, 64, 8),    # 8 per KV head, cluster of 5
     (1024, 8, 8),    # 1 per KV head, cluster of 8
-    (1025, 32, 8),   # 9 key blocks: splits through the workspace, partial last block
+    (1025, 32, 8),   # 9 key blocks: cluster of 5 with two blocks each (two-stage ring),
+                     # the last CTA one partial block
+    (2048, 32, 8),   # 16 key blocks: cluster of 8 with two blocks each
+    (2200, 32, 8),   # 18 key blocks: one-block splits through the workspace
     (3000, 16, 1),   # 16 query heads on one KV head (the widest group the MMA takes)
     (300, 32, 1)])   # 32 per KV head: beyond the tcgen05 decode, the bulk kernel
 def test_decode_tcgen05_groups_and_splits(pkg, dev, kv_len, h, h_kv):
