@@ -183,11 +183,11 @@ ENGINE_B200_API int engine_cuda_rmsnorm_linear_f16(const engine_half_t* x, const
  * call allocates nothing: for serving loops that reserve all device memory at
  * start-up and may not allocate per request, and for hosts whose device memory
  * is owned by another allocator.  It always takes the tensor-core path with
- * hi/lo activations formed by a pre-pass into that array; the result agrees
- * with engine_cuda_rmsnorm_linear_f16's within rounding (both inside the FP32
- * bound): for M <= 4 that entry point uses the CUDA-core GEMV, and for
- * 5 <= M <= 32 it builds the activations inside the GEMM and applies the RMS
- * scale to the FP32 result.
+ * hi/lo activations formed by a pre-pass into that array.  For 5 <= M <= 32
+ * engine_cuda_rmsnorm_linear_f16 runs the same pre-pass (into pool memory) and
+ * the same GEMM, so the results are identical; for M <= 4 it streams W on CUDA
+ * cores instead, and the two agree within rounding (both inside the FP32
+ * bound).
  * Limits: 1 <= M <= 32, K <= 16384, K a multiple of 8, W 16-byte aligned;
  * larger sizes return ENGINE_ERR_UNSUPPORTED.  Make one warm-up call per device
  * at start-up: it looks up the array's device address, and with lazy module
