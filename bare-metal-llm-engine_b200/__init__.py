@@ -82,6 +82,8 @@ EXPORTS: dict[str, list] = {
     "engine_cuda_kv_cache_write": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "engine_cuda_kv_cache_write_rows": [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                         _p],
+    "engine_cuda_rmsnorm_linear_kv_f16": [_p, _p, _p, _p, _p, _i64, _i64, _f, _p, _p, _i64, _i64,
+                                          _i64, _i64, _i64, _p],
     "engine_gguf_open": [ctypes.c_char_p, _P(ctypes.c_void_p)],
     "engine_gguf_close": [_p],
     "engine_gguf_version": [_p, _P(ctypes.c_int32), _P(ctypes.c_uint64)],

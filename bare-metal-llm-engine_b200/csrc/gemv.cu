@@ -72,6 +72,16 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
   }
 }
 
+// KV-cache scatter of the batch-1 norm projection (engine_cuda_rmsnorm_linear_kv_f16):
+// output rows [n0, n0 + nkv) are the new token's K row and [n0 + nkv, n0 + 2 nkv)
+// its V row; each is also stored at position `pos` of its head in the caches
+// ([heads][max_len][d]: element c of head h at h * head_stride + pos_off + c).
+struct KvScatter {
+  __half* k = nullptr;
+  __half* v = nullptr;
+  int64_t n0 = 0, nkv = 0, d = 1, head_stride = 0, pos_off = 0;
+};
+
 // Batch-1 fused RMSNorm -> GEMV.  Persistent: each CTA forms t = x * gamma
 // (FP32) in shared memory and the sum of squares of x with one block reduction
 // -- once per CTA, not once per row block -- then streams row block after row
@@ -83,10 +93,12 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_vec_kernel(
 // PAIR (the SwiGLU projection): W holds 2N rows, gate rows [0, N) then up rows
 // [N, 2N).  Warp group j streams the pair (j, N + j) -- each row accumulated
 // exactly as without PAIR -- and writes swiglu(fp16(gate_j), fp16(up_j)).
+// With kv.k set, the store loop also writes the K / V rows into the caches.
 template <int RPW, int SK, int U, bool RESID, bool PAIR = false>
 __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
     const __half* __restrict__ W, const __half* __restrict__ X, const __half* __restrict__ gamma,
-    const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps) {
+    const __half* __restrict__ R, __half* __restrict__ Y, int64_t N, int64_t K, float eps,
+    const KvScatter kv) {
   constexpr int GROUPS = kNkVecWarps / SK;
   static_assert(!PAIR || (RPW == 2 && !RESID), "PAIR streams one gate/up row pair per group");
   constexpr int64_t ROWS = static_cast<int64_t>(GROUPS) * (PAIR ? 1 : RPW);  // outputs per block
@@ -245,7 +257,16 @@ __global__ void __launch_bounds__(kNkVecWarps * 32) gemv_nk_norm1_kernel(
         for (int q = 0; q < SK; ++q) v += red[g * SK + q][r];
         v = v * scale;
         if constexpr (RESID) v = v + __half2float(R[row]);
-        Y[row] = __float2half_rn(v);
+        const __half h = __float2half_rn(v);
+        Y[row] = h;
+        if (kv.k != nullptr) {
+          const int64_t e = row - kv.n0;
+          if (e >= 0 && e < 2 * kv.nkv) {
+            const bool is_v = e >= kv.nkv;
+            const int64_t f = is_v ? e - kv.nkv : e;
+            (is_v ? kv.v : kv.k)[(f / kv.d) * kv.head_stride + kv.pos_off + f % kv.d] = h;
+          }
+        }
       }
     }
     __syncthreads();  // `red` is reused by the next row block
@@ -305,7 +326,8 @@ void launch_nk_vec(const __half* W, const __half* X, const __half* gamma, const 
 
 template <int RPW, int SK, bool RESID, bool PAIR = false>
 int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const __half* R,
-                    __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream) {
+                    __half* Y, int64_t N, int64_t K, float eps, cudaStream_t stream,
+                    const KvScatter& kv = KvScatter{}) {
   constexpr int64_t rows_per_cta = static_cast<int64_t>(kNkVecWarps / SK) * (PAIR ? 1 : RPW);
   const int64_t nblocks = (N + rows_per_cta - 1) / rows_per_cta;
   const size_t smem = static_cast<size_t>(K) * sizeof(float);
@@ -338,7 +360,7 @@ int launch_nk_norm1(const __half* W, const __half* X, const __half* gamma, const
   }
   const unsigned grid = static_cast<unsigned>(g);
   B200_CUDA(launch_pdl(kern, dim3(grid), dim3(kNkVecWarps * 32), smem, stream, W, X, gamma, R, Y,
-                       N, K, eps));
+                       N, K, eps, kv));
   return ENGINE_OK;
 }
 
@@ -729,6 +751,49 @@ int engine_cuda_gemv_f16_nk(const engine_half_t* W, const engine_half_t* x,
   return gemv_nk_f16(reinterpret_cast<const __half*>(W), reinterpret_cast<const __half*>(x),
                      nullptr, 0.f, false, reinterpret_cast<const __half*>(residual),
                      reinterpret_cast<__half*>(y), 1, N, K, stream);
+  B200_ENTRY_END
+}
+
+int engine_cuda_rmsnorm_linear_kv_f16(const engine_half_t* x, const engine_half_t* gamma,
+                                      const engine_half_t* W, const engine_half_t* residual,
+                                      engine_half_t* Y, int64_t N, int64_t K, float eps,
+                                      engine_half_t* k_cache, engine_half_t* v_cache,
+                                      int64_t kv_row0, int64_t n_kv_heads, int64_t head_dim,
+                                      int64_t max_len, int64_t pos, engine_stream_t stream) {
+  B200_ENTRY_BEGIN
+  B200_REQUIRE(N >= 0 && K >= 0, "rmsnorm_linear_kv_f16: negative dimension");
+  B200_REQUIRE(x != nullptr && W != nullptr && Y != nullptr,
+               "rmsnorm_linear_kv_f16: null device pointer");
+  B200_REQUIRE(k_cache != nullptr && v_cache != nullptr, "rmsnorm_linear_kv_f16: cache is null");
+  B200_REQUIRE(eps >= 0.0f, "rmsnorm_linear_kv_f16: eps must be non-negative");
+  B200_REQUIRE(n_kv_heads > 0 && head_dim > 0, "rmsnorm_linear_kv_f16: n_kv_heads and head_dim must be positive");
+  B200_REQUIRE(kv_row0 >= 0 && kv_row0 + 2 * n_kv_heads * head_dim <= N,
+               "rmsnorm_linear_kv_f16: the K and V rows must lie inside the N output rows");
+  B200_REQUIRE(pos >= 0 && pos < max_len, "rmsnorm_linear_kv_f16: pos must lie in [0, max_len)");
+  B200_REQUIRE(K > 0 && K % 8 == 0 && K <= 40960, "rmsnorm_linear_kv_f16: K must be a positive multiple of 8, at most 40960");
+  B200_REQUIRE(((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x) |
+                 reinterpret_cast<uintptr_t>(gamma)) % 16) == 0,
+               "rmsnorm_linear_kv_f16: W, x and gamma must be 16-byte aligned");
+  if (N == 0) return ENGINE_OK;
+  KvScatter kv;
+  kv.k = reinterpret_cast<__half*>(k_cache);
+  kv.v = reinterpret_cast<__half*>(v_cache);
+  kv.n0 = kv_row0;
+  kv.nkv = n_kv_heads * head_dim;
+  kv.d = head_dim;
+  kv.head_stride = max_len * head_dim;
+  kv.pos_off = pos * head_dim;
+  const auto* wh = reinterpret_cast<const __half*>(W);
+  const auto* xh = reinterpret_cast<const __half*>(x);
+  const auto* gh = reinterpret_cast<const __half*>(gamma);
+  const auto* rh = reinterpret_cast<const __half*>(residual);
+  auto* yh = reinterpret_cast<__half*>(Y);
+  // The batch-1 configuration of engine_cuda_rmsnorm_linear_f16 (two rows per
+  // warp group, K split over two warps), so Y is bit-identical to it.
+  const int rc = rh ? launch_nk_norm1<2, 2, true>(wh, xh, gh, rh, yh, N, K, eps, stream, kv)
+                    : launch_nk_norm1<2, 2, false>(wh, xh, gh, rh, yh, N, K, eps, stream, kv);
+  if (rc != ENGINE_OK) return rc;
+  return check_launch("rmsnorm_linear_kv_f16");
   B200_ENTRY_END
 }
 

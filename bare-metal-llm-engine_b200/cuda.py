@@ -125,6 +125,15 @@ def rmsnorm_linear_swiglu_f16(x, gamma, W_gu, Y, M, F, K, eps, stream=0):
     _check(lib().engine_cuda_rmsnorm_linear_swiglu_f16(x, gamma, W_gu, Y, M, F, K, eps, _s(stream)))
 
 
+def rmsnorm_linear_kv_f16(x, gamma, W, residual, Y, N, K, eps, k_cache, v_cache, kv_row0,
+                          n_kv_heads, head_dim, max_len, pos, stream=0):
+    """Batch-1 rmsnorm_linear_f16 that also stores output rows [kv_row0, +n_kv_heads*head_dim)
+    (K) and the next n_kv_heads*head_dim (V) at position pos of the head-major caches."""
+    _check(lib().engine_cuda_rmsnorm_linear_kv_f16(x, gamma, W, residual, Y, N, K, eps, k_cache,
+                                                   v_cache, kv_row0, n_kv_heads, head_dim,
+                                                   max_len, pos, _s(stream)))
+
+
 def rmsnorm_linear_f16_noalloc(x, gamma, W, residual, Y, M, N, K, eps, stream=0):
     """rmsnorm_linear_f16 without any device allocation (fixed in-library scratch;
     M <= 32, K <= 16384).  Concurrent calls on unordered streams race."""

@@ -100,6 +100,29 @@ def rmsnorm_linear(x, gamma, W, eps: float = 1e-5, residual=None, out=None):
     return Y
 
 
+def rmsnorm_linear_kv(x, gamma, W, eps, k_cache, v_cache, kv_row0: int, pos: int, out=None):
+    """Batch-1 rmsnorm_linear (x [1, K]) whose output rows [kv_row0, kv_row0 + H_kv*d)
+    and the next H_kv*d rows (the token's K and V) are also stored at position pos
+    of the head-major caches [H_kv, max_len, d], in the same kernel."""
+    _req(x, torch.float16, "x")
+    _req(W, torch.float16, "W")
+    if gamma is not None:
+        _req(gamma, torch.float16, "gamma")
+    for t, n in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        if t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+            raise TypeError(f"{n} must be a contiguous CUDA float16 tensor [H_kv, max_len, d]")
+    M, K = x.shape
+    if M != 1:
+        raise ValueError("rmsnorm_linear_kv: one token (x [1, K])")
+    N = W.shape[0]
+    hk, max_len, d = k_cache.shape
+    Y = out if out is not None else torch.empty(1, N, device=x.device, dtype=torch.float16)
+    _c.rmsnorm_linear_kv_f16(x.data_ptr(), _ptr(gamma), W.data_ptr(), 0, Y.data_ptr(), N, K, eps,
+                             k_cache.data_ptr(), v_cache.data_ptr(), kv_row0, hk, d, max_len, pos,
+                             _stream())
+    return Y
+
+
 def rmsnorm_linear_swiglu(x, gamma, W_gu, eps: float = 1e-5, out=None):
     """swiglu(g, u) with [g | u] = rmsnorm(x; gamma, eps) @ W_gu^T, W_gu [2F,K] = gate
     rows then up rows; FP16.  Same result as rmsnorm_linear followed by swiglu."""

@@ -140,6 +140,9 @@ class CudaOps:
     def kv_cache_write(self, k_rows, v_rows, k_cache, v_cache, pos, n_seq=1):
         self._o.kv_cache_write(k_rows, v_rows, k_cache, v_cache, pos, n_seq)
 
+    def rmsnorm_linear_kv(self, x, gamma, W, eps, k_cache, v_cache, kv_row0, pos, out=None):
+        return self._o.rmsnorm_linear_kv(x, gamma, W, eps, k_cache, v_cache, kv_row0, pos, out=out)
+
     def attention_prefill(self, q, k_cache, v_cache, kv_len, q_pos_offset):
         return self._o.attention_cached(q, k_cache, v_cache, kv_len, q_pos_offset, True)
 
@@ -260,8 +263,9 @@ class TPLayerSet:
                    for _ in self.layers]
         self.n_seq, self.max_len, self.pos = n_seq, max_len, pos
 
-    def _attention(self, qkv, li: int):
-        """Rank-local attention of one layer: qkv [rows, (hq + 2 hk) * d] -> [rows, hq * d]."""
+    def _attention(self, qkv, li: int, cached: bool = False):
+        """Rank-local attention of one layer: qkv [rows, (hq + 2 hk) * d] -> [rows, hq * d].
+        cached: the projection has already stored this token's K / V rows."""
         cfg, ops = self.cfg, self.ops
         d = cfg.head_dim
         hq = cfg.n_heads // self.world
@@ -276,7 +280,8 @@ class TPLayerSet:
                 raise ValueError(f"decode step of {rows} tokens for {self.n_seq} sequences")
             if self.pos + 1 > self.max_len:
                 raise ValueError("KV cache full")
-            ops.kv_cache_write(k_rows, v_rows, kc, vc, self.pos, n_seq=rows)
+            if not cached:
+                ops.kv_cache_write(k_rows, v_rows, kc, vc, self.pos, n_seq=rows)
             out = ops.attention_decode(q.view(rows * hq, d), kc, vc, self.pos + 1)
         else:  # prefill of one sequence: `rows` tokens from position pos
             if self.pos + rows > self.max_len:
@@ -298,10 +303,19 @@ class TPLayerSet:
         lead = self.rank == 0
         fused = (self.comm is not None and self.world > 1
                  and self.comm.fits(x.shape[0], cfg.d_model))
+        # Decode of one sequence: the Q/K/V projection stores the token's K / V
+        # rows into the caches itself (one kernel instead of two per layer).
+        fuse_kv = (self.kv is not None and x.shape[0] == 1 and self.n_seq == 1
+                   and hasattr(ops, "rmsnorm_linear_kv") and self.pos + 1 <= self.max_len)
         for li, L in enumerate(self.layers):
-            qkv = ops.rmsnorm_linear(x, L["attn_norm"], L["qkv"], cfg.eps)
+            if fuse_kv:
+                kc, vc = self.kv[li]
+                qkv = ops.rmsnorm_linear_kv(x, L["attn_norm"], L["qkv"], cfg.eps, kc, vc, qd,
+                                            self.pos)
+            else:
+                qkv = ops.rmsnorm_linear(x, L["attn_norm"], L["qkv"], cfg.eps)
             if self.kv is not None:
-                attn = self._attention(qkv, li)
+                attn = self._attention(qkv, li, cached=fuse_kv)
             else:
                 attn = qkv[:, :qd].contiguous()  # stand-in: the q-head slice
             x = self._row_split(attn, L["o"], x, lead, fused)

@@ -361,6 +361,23 @@ ENGINE_B200_API int engine_cuda_kv_cache_write_rows(const engine_half_t* k_new,
                                                     int64_t pos_offset, int64_t kv_max_seq_len,
                                                     engine_stream_t stream);
 
+/* Batch-1 decode: the fused Q/K/V projection of one token and its KV-cache
+ * write as one kernel.  Y[N] = rmsnorm(x) W^T (+ residual), exactly as
+ * engine_cuda_rmsnorm_linear_f16 with M = 1, and output rows [kv_row0,
+ * kv_row0 + n_kv_heads * head_dim) (the token's K row) and the next
+ * n_kv_heads * head_dim rows (its V row) are also stored at position pos of
+ * head-major caches [n_kv_heads][max_len][head_dim] -- what
+ * engine_cuda_kv_cache_write of those rows would store.  No counterpart in the
+ * reference: it fuses rmsnorm_linear (kernels.hpp:97) with detail::kv_cache_write
+ * (kernels.hpp:184) and saves the write's launch in every layer of a decode
+ * step.  Needs K a positive multiple of 8 (at most 40960) and 16-byte aligned
+ * W, x and gamma (gamma may be null: unit gains). */
+ENGINE_B200_API int engine_cuda_rmsnorm_linear_kv_f16(
+    const engine_half_t* x, const engine_half_t* gamma, const engine_half_t* W,
+    const engine_half_t* residual, engine_half_t* Y, int64_t N, int64_t K, float eps,
+    engine_half_t* k_cache, engine_half_t* v_cache, int64_t kv_row0, int64_t n_kv_heads,
+    int64_t head_dim, int64_t max_len, int64_t pos, engine_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * GGUF model files, memory-mapped, feeding the projections.  The engine plans a
  * GGUF-style mmap'd loader (README.md:247, Module 7; tensor.hpp:19-23: weight

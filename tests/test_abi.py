@@ -265,6 +265,24 @@ def test_kv_cache_write_entries_reject_bad_arguments(pkg):
     c.kv_cache_write_rows(0, 0, 128, 0, 0, 0, 3, 1, 128, 0, 4)  # no sequences: no-op
 
 
+def test_rmsnorm_linear_kv_rejects_bad_arguments(pkg):
+    """The fused batch-1 projection + KV-cache store checks its arguments before
+    any launch: dimensions, null pointers, the K / V rows inside the N outputs,
+    the position inside the cache, K and the 16-byte alignment the kernel needs."""
+    c = pkg.cuda
+    f = c.rmsnorm_linear_kv_f16
+    # x, gamma, W, residual, Y, N, K, eps, k_cache, v_cache, kv_row0, n_kv_heads, head_dim, max_len, pos
+    _throws(pkg, f, P, P, P, 0, P, -1, 4096, 1e-5, P, P, 4096, 8, 128, 16, 0, substr="negative dimension")
+    _throws(pkg, f, 0, P, P, 0, P, 6144, 4096, 1e-5, P, P, 4096, 8, 128, 16, 0, substr="null device pointer")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4096, 1e-5, 0, P, 4096, 8, 128, 16, 0, substr="cache is null")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4096, -1.0, P, P, 4096, 8, 128, 16, 0, substr="eps")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4096, 1e-5, P, P, 4096, 0, 128, 16, 0, substr="positive")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4096, 1e-5, P, P, 4100, 8, 128, 16, 0, substr="inside the N")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4096, 1e-5, P, P, 4096, 8, 128, 16, 16, substr="pos must")
+    _throws(pkg, f, P, P, P, 0, P, 6144, 4100, 1e-5, P, P, 4096, 8, 128, 16, 0, substr="multiple of 8")
+    _throws(pkg, f, P + 2, P, P, 0, P, 6144, 4096, 1e-5, P, P, 4096, 8, 128, 16, 0, substr="aligned")
+
+
 def test_c_abi_links_and_runs_from_plain_c(pkg, tmp_path):
     """include/engine_b200.h is C99 (pedantic, warnings as errors), and a plain C
     program links libengine_b200.so and makes calls that need no GPU: the ABI

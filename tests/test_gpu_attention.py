@@ -266,6 +266,43 @@ def test_kv_cache_write_scatter_is_exact(pkg, dev, n_seq, s_new, h_kv, d, pitch_
     assert np.array_equal(vc.cpu().numpy().view(np.uint16), want_v.view(np.uint16))
 
 
+@pytest.mark.parametrize("N,K,kv_row0,h_kv,d,max_len,pos,gamma,resid", [
+    (6144, 4096, 4096, 8, 128, 40, 17, True, False),   # Llama-3-8B Q/K/V, t = 1
+    (768, 4096, 512, 1, 128, 16, 0, True, True),       # the t = 8 shard, residual
+    (1536, 4096, 1024, 2, 128, 9, 8, False, False),    # t = 4 shard, unit gains, last slot
+    (100, 64, 20, 5, 8, 3, 2, True, False)])           # small heads, the V rows end at row N
+def test_rmsnorm_linear_kv_equals_projection_then_cache_write(pkg, dev, N, K, kv_row0, h_kv, d,
+                                                              max_len, pos, gamma, resid):
+    """engine_cuda_rmsnorm_linear_kv_f16 (the batch-1 Q/K/V projection that stores
+    the token's K / V rows itself) against rmsnorm_linear_f16 at M = 1 followed
+    by kv_cache_write of those rows: Y and both caches bit for bit, every other
+    cache position untouched."""
+    rng = np.random.default_rng(N + K + pos)
+    x = torch.from_numpy(rng.standard_normal((1, K)).astype(np.float16)).to(dev)
+    g = torch.from_numpy((1 + 0.1 * rng.standard_normal(K)).astype(np.float16)).to(dev) if gamma else None
+    W = torch.from_numpy((rng.standard_normal((N, K)) * 0.02).astype(np.float16)).to(dev)
+    R = torch.from_numpy(rng.standard_normal((1, N)).astype(np.float16)).to(dev) if resid else None
+    kc0 = torch.from_numpy(rng.standard_normal((h_kv, max_len, d)).astype(np.float16)).to(dev)
+    vc0 = torch.from_numpy(rng.standard_normal((h_kv, max_len, d)).astype(np.float16)).to(dev)
+    kc, vc = kc0.clone(), vc0.clone()
+    Y = torch.empty(1, N, device=dev, dtype=torch.float16)
+    gp = g.data_ptr() if g is not None else 0
+    rp = R.data_ptr() if R is not None else 0
+    pkg.cuda.rmsnorm_linear_kv_f16(x.data_ptr(), gp, W.data_ptr(), rp, Y.data_ptr(), N, K, 1e-5,
+                                   kc.data_ptr(), vc.data_ptr(), kv_row0, h_kv, d, max_len, pos)
+    Y2 = torch.empty(1, N, device=dev, dtype=torch.float16)
+    pkg.cuda.rmsnorm_linear_f16(x.data_ptr(), gp, W.data_ptr(), rp, Y2.data_ptr(), 1, N, K, 1e-5)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    n = h_kv * d
+    pkg.ops.kv_cache_write(Y2[:, kv_row0:kv_row0 + n], Y2[:, kv_row0 + n:kv_row0 + 2 * n], kc2, vc2,
+                           pos, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(Y.view(torch.int16), Y2.view(torch.int16))
+    assert torch.equal(kc.view(torch.int16), kc2.view(torch.int16))
+    assert torch.equal(vc.view(torch.int16), vc2.view(torch.int16))
+    assert not torch.equal(kc[:, pos], kc0[:, pos])  # the slot was written
+
+
 @pytest.mark.parametrize("B,H,Hk,kv,max_len,check", [
     (3, 8, 2, 700, 800, (0, 1, 2)),       # 6 KV heads: each split one block, merged in a cluster
     (40, 32, 8, 1000, 1024, (0, 39))])    # 320 KV heads: one CTA per head streams 8 blocks

@@ -45,6 +45,16 @@ class CpuOps:
         self.calls.append("embedding")
         return table[ids.long()].double()
 
+    def rmsnorm_linear_kv(self, x, gamma, W, eps, k_cache, v_cache, kv_row0, pos, out=None):
+        """The batch-1 projection that also stores the token's K / V rows at pos."""
+        y = self.rmsnorm_linear(x, gamma, W, eps)
+        self.calls[-1] = "rmsnorm_linear_kv"
+        hk, _, d = k_cache.shape
+        n = hk * d
+        k_cache[:, pos] = y[0, kv_row0:kv_row0 + n].reshape(hk, d)
+        v_cache[:, pos] = y[0, kv_row0 + n:kv_row0 + 2 * n].reshape(hk, d)
+        return y
+
     # -- attention over head-major caches [n_seq * H_kv, max_len, d]
 
     def kv_cache_write(self, k_rows, v_rows, k_cache, v_cache, pos, n_seq=1):
